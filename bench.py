@@ -1,0 +1,320 @@
+"""Benchmark of the DSALT attention forward core on B200 (BASELINE.json's metric).
+
+Workload: one DSALT layer, B=1, L=131072, H=16, head_dim 64, d_model 1024,
+window widths in [16, 512] from the random-init predictor, k=128 landmarks, block-causal
+selection over 512-query blocks, bf16. Inputs are synthetic: x ~ N(0,1), weights
+N(0, 0.02), seeded; q/k/v come from the layer's projections and RoPE (library GEMMs,
+outside the timed region). A step is the core of the layer's inference forward: window
+widths + selection signals, block-causal landmark selection, sparse attention.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+One JSON line on rank 0. ``value`` is the device-timed step throughput (tokens/s, all
+ranks), ``e2e`` the same metric through the C-ABI call with host buffers (pinned
+host→device copies of x, q, k, v and the device→host copy of the output inside the
+timed region), ``roofline`` the attention kernel's achieved HBM bandwidth against
+MEASURED_PEAKS.json, ``cpu_baseline`` the reference's CPU path on a bounded sample.
+With N > 1 every rank runs its own L=131072 instance (independent replicas, weak
+scaling) — the sequence-sharded path is reported separately.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(workload="dsalt_attn_fwd_core_L131072_H16_D64_k128_block512_bf16", L=131072, H=16, D=64, dm=1024,
+           n_min=16, n_max=512, k=128, block=512)
+METRIC = "DSALT attn fwd tokens/s at L=131072"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def make_inputs(dev, seed=0):
+    from dsalt_b200.module import apply_rotary_emb, build_rope_cache
+    T, H, D, dm = CFG["L"], CFG["H"], CFG["D"], CFG["dm"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, dm, device=dev, generator=g).bfloat16()
+
+    def w(*s):
+        return (torch.randn(*s, device=dev, generator=g) * 0.02).bfloat16()
+
+    Wq, Wk, Wv, gw = w(dm, dm), w(dm, dm), w(dm, dm), w(dm)
+    gb = torch.zeros(1, device=dev).bfloat16()
+    alpha = torch.sigmoid(torch.full((H,), 0.4054651081081644, device=dev)).float()
+    q = (x @ Wq.T).view(T, H, D)
+    k = (x @ Wk.T).view(T, H, D)
+    v = (x @ Wv.T).view(T, H, D).contiguous()
+    cos, sin = build_rope_cache(T, D, dev)
+    q, k = apply_rotary_emb(q, k, cos.bfloat16().unsqueeze(1), sin.bfloat16().unsqueeze(1))
+    return x, gw, gb, alpha, q.contiguous(), k.contiguous(), v
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples taken during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(x, gw, gb, alpha, q, k, v, budget_s=12.0):
+    """The reference's block-causal CPU path on a sample of blocks spread along L."""
+    from dsalt_b200 import ops
+    from oracle.cpu_baseline import BlockCausalCPU
+    T, B = CFG["L"], CFG["block"]
+    w, xn, vn = ops.window_signals(x, gw, gb, CFG["n_min"], CFG["n_max"], v.view(T, -1), CFG["D"])
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    base = BlockCausalCPU(q.float().cpu(), k.float().cpu(), v.float().cpu(), w.cpu(), xn.cpu(), vn.cpu(),
+                          alpha.cpu(), CFG["k"], B)
+    nb = T // B
+    base.run_block(nb // 2)  # warm-up
+    order = [int(round(i * (nb - 1) / 31)) for i in range(32)]
+    done, tok, spent = [], 0, 0.0
+    for b in order:
+        t, dt = base.time_sample([b])
+        done.append(b)
+        tok += t
+        spent += dt
+        if spent > budget_s:
+            break
+    return {"value": tok / spent, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{len(done)} of {nb} 512-query blocks spread over L=131072 (select + attention, fp32 "
+                      f"torch CPU restatement of the reference's block-causal path), {spent:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    if dev is None:
+        print(json.dumps({"impl": "reference", "unavailable": "no CUDA device to build the synthetic inputs"}))
+        return
+    x, gw, gb, alpha, q, k, v = make_inputs(dev)
+    vals = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(x, gw, gb, alpha, q, k, v, budget_s=6.0 if i >= args.warmup else 2.0)
+        if i >= args.warmup:
+            vals.append(r["value"])
+            base = r
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": CFG["L"] / value * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": CFG["workload"], "where": "host CPU cores"},
+            "cpu_baseline": {**base, "value": value},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from dsalt_b200 import ops
+    T, H, D, k, B = CFG["L"], CFG["H"], CFG["D"], CFG["k"], CFG["block"]
+    x, gw, gb, alpha, q, kk, v = make_inputs(dev, seed=rank)
+    cu = [0, T]
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    out = torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(ops.core_workspace_bytes(T, 1, T, H, H, D, k, "block_causal", B), dtype=torch.uint8,
+                     device=dev)
+
+    def step():
+        ops.core_forward(x, gw, gb, CFG["n_min"], CFG["n_max"], alpha, q, kk, v, k, cu_t, mode="block_causal",
+                         block=B, cu_list=cu, workspace=ws, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    value = T * world / (ms / 1e3)
+    status = ops.device_status()
+
+    # dominant kernel: the attention alone on the step's widths and landmark sets
+    _, w_i, lmk_i = ops.core_forward(x, gw, gb, CFG["n_min"], CFG["n_max"], alpha, q, kk, v, k, cu_t,
+                                     mode="block_causal", block=B, cu_list=cu, return_aux=True)
+    n_att = max(20, args.steps // 4)
+    for _ in range(3):
+        ops.dsalt_attention(q, kk, v, lmk_i, None, w_i, cu_t, lmk_block=B, out_dtype=torch.bfloat16, cu_list=cu)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(n_att):
+        ops.dsalt_attention(q, kk, v, lmk_i, None, w_i, cu_t, lmk_block=B, out_dtype=torch.bfloat16, cu_list=cu)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    att_ms = e0.elapsed_time(e1) / n_att
+    att_bytes = 4 * T * H * D * 2  # q, k, v read once + output written once (bf16)
+    hbm, src = peaks()
+    achieved = att_bytes / (att_ms / 1e3) / 1e9
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "attn_fwd_tc_L131072.json")
+    if os.path.exists(prof):
+        try:
+            traffic = json.load(open(prof)).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    # end to end through the C-ABI call with host buffers
+    xh = x.cpu().pin_memory()
+    qh, kh, vh = q.cpu().pin_memory(), kk.cpu().pin_memory(), v.cpu().pin_memory()
+    oh = torch.empty(T, H, D, dtype=torch.bfloat16).pin_memory()
+    xd, qd, kd, vd = torch.empty_like(x), torch.empty_like(q), torch.empty_like(kk), torch.empty_like(v)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        ops.core_forward(xd, gw, gb, CFG["n_min"], CFG["n_max"], alpha, qd, kd, vd, k, cu_t, mode="block_causal",
+                         block=B, cu_list=cu, workspace=ws, out=out)
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps, world)
+    h2d = sum(t.numel() * t.element_size() for t in (xh, qh, kh, vh))
+    d2h = oh.numel() * oh.element_size()
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": CFG["workload"], "L": T, "heads": H, "head_dim": D, "d_model": CFG["dm"],
+                           "k_lmk": k, "block": B, "n_min": CFG["n_min"], "n_max": CFG["n_max"],
+                           "selection": "block_causal", "l2": "inputs larger than L2 (1.3 GB per step)",
+                           "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                "clocks": clk.summary(), "device_status": status,
+                "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "roofline": {"bound": "hbm", "kernel": "attn_fwd_tc_kernel", "achieved": achieved, "peak": hbm,
+                             "peak_source": src, "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
+                             "algorithmic_bytes": att_bytes, "kernel_ms": att_ms},
+                "step_breakdown_ms": {"attention": att_ms, "signals_and_selection": ms - att_ms},
+                "gpu_launches": 11 * args.steps}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(x, gw, gb, alpha, q, kk, v)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,220 @@
+// C-ABI entry points (include/dsalt_b200.h): argument checks, workspace carving, and
+// the fused core pipeline. No device memory is allocated here.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace dsalt {
+
+int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride, const void* gate_w,
+                         const void* gate_b, int gate_dtype, int n_min, int n_max, const void* v, int v_dtype,
+                         int64_t v_stride, int n_kv, int head_dim, int norm_mode, int32_t* w_out, float* xnorm_out,
+                         float* vnorm_out, float* logit_out, cudaStream_t stream);
+size_t select_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv, int k,
+                              int block);
+int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                  const int32_t* cu, int n_seqs, int64_t T, int max_seqlen, int n_heads, int n_kv, int k, int block,
+                  int32_t* lmk_out, float* zx_out, float* zv_out, void* workspace, size_t ws_bytes,
+                  cudaStream_t stream);
+int select_set_up_attributes();
+int launch_attn_f32(const float* q, const float* k, const float* v, int64_t T, int H, int Hkv, int D,
+                    int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
+                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, const int32_t* set_base, float scale,
+                    void* out, int out_dtype, float* lse, cudaStream_t stream);
+int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int HD,
+                   int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
+                   int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, int32_t* set_base, int32_t* tile_base,
+                   void* out, int out_dtype, float* lse, int* err, cudaStream_t stream);
+int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream);
+
+// ---------------------------------------------------------------- errors
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return DSALT_OK;
+  return fail(DSALT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// device status word (one per device, lives in this library's module)
+__device__ int g_device_status;
+
+int* device_status_ptr() {
+  static std::mutex mu;
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    ptrs[dev] = reinterpret_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+static bool valid_dtype(int dt) { return dt == DSALT_F32 || dt == DSALT_BF16 || dt == DSALT_F16; }
+static inline size_t a256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+}  // namespace dsalt
+
+using namespace dsalt;
+
+extern "C" {
+
+const char* dsalt_last_error(void) { return g_err; }
+
+int dsalt_version(void) { return 1; }
+
+int dsalt_device_status(int* status_out, int clear, void* stream) {
+  if (!status_out) return fail(DSALT_ERR_INVALID, "device_status: null output");
+  int* p = device_status_ptr();
+  if (!p) return fail(DSALT_ERR_CUDA, "device_status: symbol address unavailable");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc = check_cuda(cudaMemcpyAsync(status_out, p, sizeof(int), cudaMemcpyDeviceToHost, s), "device_status read");
+  if (rc) return rc;
+  if (clear) {
+    rc = check_cuda(cudaMemsetAsync(p, 0, sizeof(int), s), "device_status clear");
+    if (rc) return rc;
+  }
+  return check_cuda(cudaStreamSynchronize(s), "device_status sync");
+}
+
+int dsalt_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride, const void* gate_w,
+                        const void* gate_b, int gate_dtype, int n_min, int n_max, const void* v, int v_dtype,
+                        int64_t v_stride, int n_kv, int head_dim, int norm_mode, int32_t* w_out, float* xnorm_out,
+                        float* vnorm_out, float* logit_out, void* stream) {
+  return launch_token_signals(x, x_dtype, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_dtype,
+                              v_stride, n_kv, head_dim, norm_mode, w_out, xnorm_out, vnorm_out, logit_out,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dsalt_select_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv, int k,
+                                    int block) {
+  return select_workspace_bytes(mode, T, n_seqs, max_seqlen, n_heads, n_kv, k, block);
+}
+
+int dsalt_select_landmarks(int mode, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                           const int32_t* cu_seqlens, int n_seqs, int64_t T, int max_seqlen, int n_heads, int n_kv,
+                           int k, int block, int32_t* lmk_out, float* zx_out, float* zv_out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  return launch_select(mode, xnorm, vnorm, w, alpha, cu_seqlens, n_seqs, T, max_seqlen, n_heads, n_kv, k, block,
+                       lmk_out, zx_out, zv_out, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dsalt_attention_workspace_bytes(int64_t T, int n_seqs, int n_heads, int k_lmk, int lmk_block) {
+  (void)T;
+  (void)n_heads;
+  (void)k_lmk;
+  (void)lmk_block;
+  if (n_seqs < 1) return 0;
+  return 2 * a256(sizeof(int32_t) * (size_t)(n_seqs + 1));
+}
+
+int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
+                        int head_dim, int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk,
+                        const float* lmk_bias, int k_lmk, int lmk_block, const int32_t* cu_seqlens, int n_seqs,
+                        int max_seqlen, void* out, int out_dtype, float* lse, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  (void)max_seqlen;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (T < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || head_dim < 1 || n_seqs < 1 || k_lmk < 0 ||
+      lmk_block < 0)
+    return fail(DSALT_ERR_INVALID, "attention: bad sizes");
+  if (!valid_dtype(dtype) || !valid_dtype(out_dtype)) return fail(DSALT_ERR_INVALID, "attention: dtype");
+  if (q_stride < (int64_t)n_heads * head_dim || kv_stride < (int64_t)n_kv * head_dim)
+    return fail(DSALT_ERR_INVALID, "attention: token stride smaller than heads x head_dim");
+  if (T == 0) return DSALT_OK;
+  if (!q || !k || !v || !w || !cu_seqlens || !out || (k_lmk > 0 && !lmk) || !workspace)
+    return fail(DSALT_ERR_INVALID, "attention: null pointer");
+  if (T > 0x7fffff00LL) return fail(DSALT_ERR_UNSUPPORTED, "attention: T too large");
+  const size_t need = dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k_lmk, lmk_block);
+  if (workspace_bytes < need) return fail(DSALT_ERR_WORKSPACE, "attention: workspace %zu < %zu", workspace_bytes, need);
+  int32_t* set_base = reinterpret_cast<int32_t*>(workspace);
+  int32_t* tile_base = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) +
+                                                  a256(sizeof(int32_t) * (size_t)(n_seqs + 1)));
+  if (dtype == DSALT_F32) {
+    int rc = DSALT_OK;
+    if (lmk_block > 0 && (rc = launch_chunk_table(cu_seqlens, n_seqs, lmk_block, set_base, s))) return rc;
+    return launch_attn_f32(reinterpret_cast<const float*>(q), reinterpret_cast<const float*>(k),
+                           reinterpret_cast<const float*>(v), T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk,
+                           lmk_bias, k_lmk, lmk_block, cu_seqlens, n_seqs, set_base,
+                           (float)(1.0 / sqrt((double)head_dim)), out, out_dtype, lse, s);
+  }
+  return launch_attn_tc(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
+                        lmk_block, cu_seqlens, n_seqs, set_base, tile_base, out, out_dtype, lse, device_status_ptr(),
+                        s);
+}
+
+size_t dsalt_core_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv,
+                                  int head_dim, int k, int block) {
+  (void)head_dim;
+  if (T < 0 || n_seqs < 1) return 0;
+  const int64_t n_sets_max = mode == DSALT_SELECT_GLOBAL ? n_seqs : (block > 0 ? T / block + n_seqs : 0);
+  size_t off = 0;
+  off += a256(sizeof(int32_t) * (size_t)T);                           // widths
+  off += a256(sizeof(float) * (size_t)T);                             // x norms
+  off += a256(sizeof(float) * (size_t)T * n_kv);                      // value norms
+  off += a256(sizeof(int32_t) * (size_t)n_heads * n_sets_max * k);    // landmark sets
+  off += a256(dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k, block));
+  off += a256(select_workspace_bytes(mode, T, n_seqs, max_seqlen, n_heads, n_kv, k, block));
+  return off;
+}
+
+int dsalt_core_forward(int mode, const void* x, int x_dtype, int d_model, int64_t x_stride, const void* gate_w,
+                       const void* gate_b, int gate_dtype, int n_min, int n_max, const float* alpha, int norm_mode,
+                       const void* q, const void* k, const void* v, int qkv_dtype, int n_heads, int n_kv,
+                       int head_dim, int64_t q_stride, int64_t kv_stride, int k_lmk, int block,
+                       const int32_t* cu_seqlens, int n_seqs, int64_t T, int max_seqlen, void* out, int out_dtype,
+                       int32_t* w_out, int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (mode != DSALT_SELECT_GLOBAL && mode != DSALT_SELECT_BLOCK_CAUSAL) return fail(DSALT_ERR_INVALID, "core: mode");
+  if (T < 0 || n_seqs < 1) return fail(DSALT_ERR_INVALID, "core: bad sizes");
+  if (T == 0) return DSALT_OK;
+  const size_t need = dsalt_core_workspace_bytes(mode, T, n_seqs, max_seqlen, n_heads, n_kv, head_dim, k_lmk, block);
+  if (!workspace || workspace_bytes < need) return fail(DSALT_ERR_WORKSPACE, "core: workspace %zu < %zu", workspace_bytes, need);
+  const int64_t n_sets_max = mode == DSALT_SELECT_GLOBAL ? n_seqs : T / block + n_seqs;
+  char* ws = reinterpret_cast<char*>(workspace);
+  size_t off = 0;
+  int32_t* w = w_out ? w_out : reinterpret_cast<int32_t*>(ws + off);
+  off += a256(sizeof(int32_t) * (size_t)T);
+  float* xn = reinterpret_cast<float*>(ws + off);
+  off += a256(sizeof(float) * (size_t)T);
+  float* vn = reinterpret_cast<float*>(ws + off);
+  off += a256(sizeof(float) * (size_t)T * n_kv);
+  int32_t* lmk = lmk_out ? lmk_out : reinterpret_cast<int32_t*>(ws + off);
+  off += a256(sizeof(int32_t) * (size_t)n_heads * n_sets_max * k_lmk);
+  void* aws = ws + off;
+  const size_t aws_bytes = a256(dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k_lmk, block));
+  off += aws_bytes;
+  void* sws = ws + off;
+  const size_t sws_bytes = workspace_bytes - off;
+  int rc = dsalt_token_signals(x, x_dtype, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v,
+                               qkv_dtype, kv_stride, n_kv, head_dim, norm_mode, w, xn, vn, nullptr, stream);
+  if (rc) return rc;
+  rc = dsalt_select_landmarks(mode, xn, vn, w, alpha, cu_seqlens, n_seqs, T, max_seqlen, n_heads, n_kv, k_lmk, block,
+                              lmk, nullptr, nullptr, sws, sws_bytes, stream);
+  if (rc) return rc;
+  return dsalt_attention_fwd(q, k, v, qkv_dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, nullptr,
+                             k_lmk, mode == DSALT_SELECT_GLOBAL ? 0 : block, cu_seqlens, n_seqs, max_seqlen, out,
+                             out_dtype, nullptr, aws, aws_bytes, stream);
+  (void)s;
+}
+
+}  // extern "C"

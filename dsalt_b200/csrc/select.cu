@@ -1,0 +1,811 @@
+// Landmark selection kernels.
+//
+// Whole-sequence mode follows dsalt/kernels/selectors.py:75-134 with the score of
+// dsalt/kernels/landmark_tokens_ker.py:47-60: mean/std of ‖x‖ and of each kv group's
+// value norm over all packed tokens, s = α·z_v + (1−α)·z_x, tokens inside their own
+// window (seq_off < w) excluded, top-k per (head, sequence).
+//
+// Block-causal mode follows results/causal_landmark_check.py:82-113 (driven per block at
+// :176-186): for block b of a sequence the candidates are positions [0, b·B) and the
+// statistics are those of that prefix (float64 mean, unbiased std, clamp 1e-6; z cast to
+// fp32); blocks with fewer than two prefix tokens select nothing.
+//
+// Exactness: sums are double-double (the correctly rounded float64 of the exact sum);
+// every other op replays the reference's IEEE op chain; ties go to the lower position.
+//
+// Block-causal pruning (exact): a candidate j is never among the top-k of any block if at
+// least k uncovered tokens i < j have strictly larger value norm AND strictly larger
+// x-norm — the fp32 score is non-decreasing in both signals for α ∈ [0,1], and ties go to
+// the lower position. Tokens are binned on a 32x32 grid of thresholds; per block-sized
+// chunk a 2-D suffix histogram of earlier chunks gives a lower bound on that count, and
+// only tokens whose bound is < k remain candidates (a few thousand of 131072 on random
+// inputs). Heads whose α is outside [0,1] skip the pruning.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace dsalt {
+
+constexpr int NBIN = 32;                 // bins per signal for the dominance grid
+constexpr int NCELL = NBIN * NBIN;
+constexpr int GCHUNK = 4096;             // positions per CTA in whole-sequence phase 1
+constexpr int STAT_CHUNK = 512;          // tokens per partial sum in whole-sequence mode
+constexpr int SEL_THREADS = 512;
+constexpr int KEY_CAP = 8192;            // candidate keys cached in shared memory
+constexpr int MAX_K = 1024;
+
+// thresholds (in units of the sequence's std above its mean) of the dominance grid:
+// coarse below the mean, fine in the upper tail where the top-k lives.
+__constant__ float c_bin_t[NBIN - 1];
+
+// ---------------------------------------------------------------------------
+// sequence tables
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int find_seq(const int32_t* base, int n_seqs, int idx) {
+  int lo = 0, hi = n_seqs;  // base[0] = 0 <= idx < base[n_seqs]
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (base[mid] <= idx) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// base[s] = Σ_{s'<s} ceil(L_s'/C); one CTA.
+__global__ void chunk_table_kernel(const int32_t* __restrict__ cu, int n_seqs, int C, int32_t* __restrict__ base) {
+  __shared__ int32_t warp_tot[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int s0 = 0; s0 < n_seqs; s0 += blockDim.x) {
+    const int s = s0 + threadIdx.x;
+    int v = 0;
+    if (s < n_seqs) {
+      int L = cu[s + 1] - cu[s];
+      v = L > 0 ? (L + C - 1) / C : 0;
+    }
+    // block inclusive scan
+    int x = v;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      int t = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const int excl = carry + (wid ? warp_tot[wid - 1] : 0) + x - v;
+    if (s < n_seqs) base[s] = excl;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = excl + v;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) base[n_seqs] = carry;
+}
+
+int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream) {
+  chunk_table_kernel<<<1, 1024, 0, stream>>>(cu, n_seqs, C, base);
+  return check_cuda(cudaGetLastError(), "sequence table launch");
+}
+
+// ---------------------------------------------------------------------------
+// per-chunk double-double sums of each signal and of its square
+// signal 0 = ‖x‖, signal 1+g = value norm of kv group g
+// ---------------------------------------------------------------------------
+struct Partial {
+  double s1h, s1l, s2h, s2l;
+};
+
+__device__ __forceinline__ DD block_dd_sum(DD v, DD* red) {
+  v = dd_warp_sum(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  DD r = DD{0.0, 0.0};
+  if (wid == 0) {
+    r = lane < nw ? red[lane] : DD{0.0, 0.0};
+    r = dd_warp_sum(r);
+  }
+  return r;  // valid in thread 0
+}
+
+__global__ void chunk_sums_kernel(const float* __restrict__ xn, const float* __restrict__ vn, int n_kv,
+                                  const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
+                                  Partial* __restrict__ part) {
+  __shared__ DD red1[32], red2[32];
+  const int c = blockIdx.x, sig = blockIdx.y, nsig = 1 + n_kv;
+  const int total = base[n_seqs];
+  Partial out{0.0, 0.0, 0.0, 0.0};
+  if (c < total) {
+    const int s = find_seq(base, n_seqs, c);
+    const int lc = c - base[s];
+    const int a = cu[s] + lc * C;
+    const int b = min(cu[s + 1], a + C);
+    DD s1{0.0, 0.0}, s2{0.0, 0.0};
+    for (int t = a + threadIdx.x; t < b; t += blockDim.x) {
+      const double v = (double)(sig == 0 ? xn[t] : vn[(int64_t)t * n_kv + sig - 1]);
+      s1 = dd_add_d(s1, v);
+      s2 = dd_add_d(s2, __dmul_rn(v, v));  // exact: the square of an fp32 value fits a double
+    }
+    DD r1 = block_dd_sum(s1, red1);
+    DD r2 = block_dd_sum(s2, red2);
+    out = Partial{r1.hi, r1.lo, r2.hi, r2.lo};
+  }
+  if (threadIdx.x == 0) part[(int64_t)c * nsig + sig] = out;
+}
+
+// ---------------------------------------------------------------------------
+// whole-sequence statistics: fp32 mean and unbiased std (clamp 1e-6) over all T tokens
+//   mean = fl32(S1/n); var = (S2 − (S1/n)·S1)/(n−1); std = fl32(sqrt(var))
+// ---------------------------------------------------------------------------
+__global__ void global_stats_kernel(const Partial* __restrict__ part, int n_chunks, int nsig, int64_t T,
+                                    float* __restrict__ gstats) {
+  __shared__ DD red1[32], red2[32];
+  const int sig = blockIdx.x;
+  DD s1{0.0, 0.0}, s2{0.0, 0.0};
+  for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
+    const Partial p = part[(int64_t)c * nsig + sig];
+    s1 = dd_add(s1, DD{p.s1h, p.s1l});
+    s2 = dd_add(s2, DD{p.s2h, p.s2l});
+  }
+  DD r1 = block_dd_sum(s1, red1);
+  DD r2 = block_dd_sum(s2, red2);
+  if (threadIdx.x == 0) {
+    const double S1 = dd_round(r1), S2 = dd_round(r2);
+    const double n = (double)T;
+    const double m64 = __ddiv_rn(S1, n);
+    float stdv;
+    if (T > 1) {
+      const double var = __ddiv_rn(__dsub_rn(S2, __dmul_rn(m64, S1)), __dsub_rn(n, 1.0));
+      stdv = __double2float_rn(__dsqrt_rn(var > 0.0 ? var : 0.0));
+      stdv = fmaxf(stdv, 1e-6f);
+    } else {
+      stdv = __int_as_float(0x7fc00000);  // torch.std of one element is NaN
+    }
+    gstats[2 * sig] = __double2float_rn(m64);
+    gstats[2 * sig + 1] = stdv;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// block-wide top-k over 64-bit keys (0 = not a candidate), MSB-first radix select
+// ---------------------------------------------------------------------------
+struct TopkSmem {
+  unsigned int hist[256];
+  uint64_t prefix, mask;
+  int kk, done, cnt, all;
+};
+
+template <class Get>
+__device__ void block_topk_select(Get get, int N, int k, TopkSmem& sm, uint64_t& prefix_out, uint64_t& mask_out) {
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    sm.prefix = 0;
+    sm.mask = 0;
+    sm.kk = k;
+    sm.done = 0;
+    sm.all = 0;
+  }
+  __syncthreads();
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) sm.hist[i] = 0;
+    __syncthreads();
+    const uint64_t prefix = sm.prefix, mask = sm.mask;
+    for (int i = tid; i < N; i += blockDim.x) {
+      const uint64_t key = get(i);
+      if (key != 0 && (key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 0xFF], 1u);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      const int lane = tid;
+      unsigned int s = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += sm.hist[255 - 8 * lane - j];
+      unsigned int incl = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        unsigned int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const unsigned int total = __shfl_sync(0xffffffffu, incl, 31);
+      const int kk = sm.kk;
+      if (total <= (unsigned)kk) {
+        // every remaining candidate is selected
+        if (lane == 0) {
+          sm.done = 1;
+          if (shift == 56) sm.all = 1;
+        }
+      } else {
+        const unsigned ball = __ballot_sync(0xffffffffu, incl >= (unsigned)kk);
+        const int L = __ffs(ball) - 1;
+        if (lane == L) {
+          unsigned int cum = incl - s;
+          int d = 0;
+          unsigned int above = cum;
+#pragma unroll 1
+          for (int j = 0; j < 8; ++j) {
+            const int bin = 255 - 8 * lane - j;
+            const unsigned int h = sm.hist[bin];
+            if (cum + h >= (unsigned)kk) {
+              d = bin;
+              above = cum;
+              break;
+            }
+            cum += h;
+          }
+          const int nk = kk - (int)above;
+          sm.kk = nk;
+          sm.prefix = prefix | ((uint64_t)d << shift);
+          sm.mask = mask | ((uint64_t)0xFF << shift);
+          if (sm.hist[d] == (unsigned)nk) sm.done = 1;
+        }
+      }
+    }
+    __syncthreads();
+    if (sm.done) break;
+  }
+  prefix_out = sm.prefix;
+  mask_out = sm.mask;
+}
+
+__device__ __forceinline__ bool topk_selected(uint64_t key, uint64_t prefix, uint64_t mask) {
+  return key != 0 && (key & mask) >= prefix;
+}
+
+// emits the selected positions ascending, -1 padded to k
+template <class Get>
+__device__ void block_topk_positions(Get get, int N, int k, TopkSmem& sm, int32_t* sel, int32_t* __restrict__ out) {
+  uint64_t prefix, mask;
+  block_topk_select(get, N, k, sm, prefix, mask);
+  if (threadIdx.x == 0) sm.cnt = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    const uint64_t key = get(i);
+    if (topk_selected(key, prefix, mask)) {
+      const int slot = atomicAdd(&sm.cnt, 1);
+      if (slot < k) sel[slot] = key_pos(key);
+    }
+  }
+  __syncthreads();
+  const int cnt = min(sm.cnt, k);
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    if (j < cnt) {
+      const int p = sel[j];
+      int rank = 0;
+      for (int m = 0; m < cnt; ++m) rank += sel[m] < p;
+      out[rank] = p;
+    } else {
+      out[j] = -1;
+    }
+  }
+  __syncthreads();
+}
+
+// emits the selected keys (unordered), 0 padded to k
+template <class Get>
+__device__ void block_topk_keys(Get get, int N, int k, TopkSmem& sm, uint64_t* __restrict__ out) {
+  uint64_t prefix, mask;
+  block_topk_select(get, N, k, sm, prefix, mask);
+  if (threadIdx.x == 0) sm.cnt = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    const uint64_t key = get(i);
+    if (topk_selected(key, prefix, mask)) {
+      const int slot = atomicAdd(&sm.cnt, 1);
+      if (slot < k) out[slot] = key;
+    }
+  }
+  __syncthreads();
+  const int cnt = min(sm.cnt, k);
+  for (int j = cnt + threadIdx.x; j < k; j += blockDim.x) out[j] = 0;
+  __syncthreads();
+}
+
+// fp32 score of the whole-sequence mode (landmark_tokens_ker.py:47-60)
+__device__ __forceinline__ float global_score(float xnv, float vnv, float mx, float sx, float mv, float sv, float a) {
+  const float zx = __fdiv_rn(__fsub_rn(xnv, mx), sx);
+  const float zv = __fdiv_rn(__fsub_rn(vnv, mv), sv);
+  return __fadd_rn(__fmul_rn(a, zv), __fmul_rn(__fsub_rn(1.0f, a), zx));
+}
+
+// ---------------------------------------------------------------------------
+// whole-sequence phase 1: per (chunk of GCHUNK positions, head) local top-k keys
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(SEL_THREADS) global_phase1_kernel(
+    const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w,
+    const float* __restrict__ alpha, const float* __restrict__ gstats, const int32_t* __restrict__ cu, int n_seqs,
+    const int32_t* __restrict__ gbase, int n_heads, int n_kv, int k, uint64_t* __restrict__ cand, float* zx_out,
+    float* zv_out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
+  __shared__ TopkSmem sm;
+  const int gc = blockIdx.x, h = blockIdx.y;
+  const int total = gbase[n_seqs];
+  uint64_t* out = cand + ((int64_t)h * gridDim.x + gc) * k;
+  if (gc >= total) {
+    for (int j = threadIdx.x; j < k; j += blockDim.x) out[j] = 0;
+    return;
+  }
+  const int s = find_seq(gbase, n_seqs, gc);
+  const int start = cu[s];
+  const int p0 = (gc - gbase[s]) * GCHUNK;
+  const int p1 = min(cu[s + 1] - start, p0 + GCHUNK);
+  const int N = p1 - p0;
+  const int rep = n_heads / n_kv, g = h / rep;
+  const float mx = gstats[0], sx = gstats[1], mv = gstats[2 * (1 + g)], sv = gstats[2 * (1 + g) + 1];
+  const float a = alpha[h];
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    const int p = p0 + i;
+    const int64_t t = start + p;
+    const float xv = xn[t], vv = vn[t * n_kv + g];
+    const float sc = global_score(xv, vv, mx, sx, mv, sv, a);
+    keys[i] = (p < w[t]) ? 0ull : make_key(sc, p);
+    if (h == 0 && zx_out) zx_out[t] = __fdiv_rn(__fsub_rn(xv, mx), sx);
+    if (h % rep == 0 && zv_out) zv_out[t * n_kv + g] = __fdiv_rn(__fsub_rn(vv, mv), sv);
+  }
+  __syncthreads();
+  block_topk_keys([&](int i) { return keys[i]; }, N, k, sm, out);
+}
+
+// whole-sequence phase 2: merge the phase-1 keys of a sequence
+__global__ void __launch_bounds__(SEL_THREADS) global_phase2_kernel(const uint64_t* __restrict__ cand, int n_gchunks_alloc,
+                                                                    const int32_t* __restrict__ gbase, int n_seqs,
+                                                                    int k, int32_t* __restrict__ lmk_out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
+  __shared__ TopkSmem sm;
+  __shared__ int32_t sel[MAX_K];
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int c0 = gbase[s], c1 = gbase[s + 1];
+  const int N = (c1 - c0) * k;
+  const uint64_t* src = cand + ((int64_t)h * n_gchunks_alloc + c0) * k;
+  int32_t* out = lmk_out + ((int64_t)h * n_seqs + s) * k;
+  if (N <= KEY_CAP) {
+    for (int i = threadIdx.x; i < N; i += blockDim.x) keys[i] = src[i];
+    __syncthreads();
+    block_topk_positions([&](int i) { return keys[i]; }, N, k, sm, sel, out);
+  } else {
+    block_topk_positions([&](int i) { return src[i]; }, N, k, sm, sel, out);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// block-causal: prefix statistics per block and dominance-grid thresholds
+// stats[set][sig] = (mean, sd) float64 of positions [0, b·C) (_std_at,
+// causal_landmark_check.py:88-92); edges from the whole sequence's statistics.
+// ---------------------------------------------------------------------------
+__global__ void block_stats_kernel(const Partial* __restrict__ part, const int32_t* __restrict__ cu, int n_seqs,
+                                   const int32_t* __restrict__ base, int nsig, int C, double2* __restrict__ stats,
+                                   float* __restrict__ edges) {
+  __shared__ DD sc1[256], sc2[256];
+  __shared__ DD carry1, carry2;
+  const int s = blockIdx.x, sig = blockIdx.y;
+  const int c0 = base[s], nc = base[s + 1] - c0;
+  const int L = cu[s + 1] - cu[s];
+  if (threadIdx.x == 0) {
+    carry1 = DD{0.0, 0.0};
+    carry2 = DD{0.0, 0.0};
+  }
+  __syncthreads();
+  for (int t0 = 0; t0 < nc; t0 += 256) {
+    const int b = t0 + threadIdx.x;
+    DD v1{0.0, 0.0}, v2{0.0, 0.0};
+    if (b < nc) {
+      const Partial p = part[(int64_t)(c0 + b) * nsig + sig];
+      v1 = DD{p.s1h, p.s1l};
+      v2 = DD{p.s2h, p.s2l};
+    }
+    sc1[threadIdx.x] = v1;
+    sc2[threadIdx.x] = v2;
+    __syncthreads();
+    // Hillis-Steele inclusive scan
+    for (int off = 1; off < 256; off <<= 1) {
+      DD a1 = sc1[threadIdx.x], a2 = sc2[threadIdx.x];
+      if (threadIdx.x >= off) {
+        a1 = dd_add(a1, sc1[threadIdx.x - off]);
+        a2 = dd_add(a2, sc2[threadIdx.x - off]);
+      }
+      __syncthreads();
+      sc1[threadIdx.x] = a1;
+      sc2[threadIdx.x] = a2;
+      __syncthreads();
+    }
+    if (b < nc) {
+      // exclusive prefix = carry + inclusive(b-1)
+      DD e1 = carry1, e2 = carry2;
+      if (threadIdx.x > 0) {
+        e1 = dd_add(e1, sc1[threadIdx.x - 1]);
+        e2 = dd_add(e2, sc2[threadIdx.x - 1]);
+      }
+      const int n = b * C;
+      double2 st = make_double2(__int_as_float(0x7fc00000), 0.0);
+      if (n >= 2) {
+        const double S1 = dd_round(e1), S2 = dd_round(e2);
+        const double dn = (double)n;
+        const double mean = __ddiv_rn(S1, dn);
+        const double var = __ddiv_rn(__dsub_rn(S2, __dmul_rn(__dmul_rn(dn, mean), mean)), (double)max(n - 1, 1));
+        double sd = __dsqrt_rn(var > 0.0 ? var : 0.0);
+        sd = sd > 1e-6 ? sd : 1e-6;
+        st = make_double2(mean, sd);
+      }
+      stats[(int64_t)(c0 + b) * nsig + sig] = st;
+    }
+    __syncthreads();
+    if (threadIdx.x == 255) {
+      carry1 = dd_add(carry1, sc1[255]);
+      carry2 = dd_add(carry2, sc2[255]);
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    // whole-sequence mean / std: only used to place the dominance-grid thresholds
+    const double n = (double)max(L, 1);
+    const double S1 = dd_round(carry1), S2 = dd_round(carry2);
+    const double mean = S1 / n;
+    double var = (S2 - n * mean * mean) / fmax(n - 1.0, 1.0);
+    const double sd = sqrt(var > 0.0 ? var : 0.0);
+    for (int j = 0; j < NBIN - 1; ++j) edges[((int64_t)s * nsig + sig) * (NBIN - 1) + j] = (float)(mean + sd * c_bin_t[j]);
+  }
+}
+
+__device__ __forceinline__ int bin_of(float v, const float* e) {
+  int b = 0;
+#pragma unroll
+  for (int j = 0; j < NBIN - 1; ++j) b += (e[j] <= v) ? 1 : 0;
+  return b;
+}
+
+// per (chunk, kv group): 2-D suffix histogram G[a][b] = #uncovered tokens of the chunk
+// with value bin >= a and x bin >= b
+__global__ void __launch_bounds__(256) dominance_hist_kernel(
+    const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w, int n_kv,
+    const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
+    const float* __restrict__ edges, int32_t* __restrict__ G) {
+  __shared__ int32_t hist[NCELL];
+  __shared__ float ex[NBIN - 1], ev[NBIN - 1];
+  const int c = blockIdx.x, g = blockIdx.y, nsig = 1 + n_kv;
+  const int total = base[n_seqs];
+  int32_t* out = G + ((int64_t)c * n_kv + g) * NCELL;
+  if (c >= total) return;
+  const int s = find_seq(base, n_seqs, c);
+  for (int i = threadIdx.x; i < NCELL; i += blockDim.x) hist[i] = 0;
+  if (threadIdx.x < NBIN - 1) {
+    ex[threadIdx.x] = edges[((int64_t)s * nsig + 0) * (NBIN - 1) + threadIdx.x];
+    ev[threadIdx.x] = edges[((int64_t)s * nsig + 1 + g) * (NBIN - 1) + threadIdx.x];
+  }
+  __syncthreads();
+  const int start = cu[s];
+  const int p0 = (c - base[s]) * C;
+  const int p1 = min(cu[s + 1] - start, p0 + C);
+  for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+    const int64_t t = start + p;
+    if (p >= w[t]) atomicAdd(&hist[bin_of(vn[t * n_kv + g], ev) * NBIN + bin_of(xn[t], ex)], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < NBIN) {  // suffix along x bins
+    int run = 0;
+    for (int b = NBIN - 1; b >= 0; --b) {
+      run += hist[threadIdx.x * NBIN + b];
+      hist[threadIdx.x * NBIN + b] = run;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < NBIN) {  // suffix along value bins
+    int run = 0;
+    for (int a = NBIN - 1; a >= 0; --a) {
+      run += hist[a * NBIN + threadIdx.x];
+      hist[a * NBIN + threadIdx.x] = run;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NCELL; i += blockDim.x) out[i] = hist[i];
+}
+
+// exclusive prefix over the chunks of each sequence, in place: G[c] <- Σ_{c'<c} G[c']
+__global__ void dominance_scan_kernel(int32_t* __restrict__ G, const int32_t* __restrict__ base, int n_kv) {
+  const int s = blockIdx.x / n_kv, g = blockIdx.x % n_kv;
+  const int cell = blockIdx.y * blockDim.x + threadIdx.x;
+  if (cell >= NCELL) return;
+  int run = 0;
+  for (int c = base[s]; c < base[s + 1]; ++c) {
+    int32_t* p = G + ((int64_t)c * n_kv + g) * NCELL + cell;
+    const int v = *p;
+    *p = run;
+    run += v;
+  }
+}
+
+// survivors: uncovered tokens dominated (strictly, in both signals) by fewer than k
+// uncovered tokens of earlier chunks; written in position order per (chunk, group)
+__global__ void survivor_kernel(const float* __restrict__ xn, const float* __restrict__ vn,
+                                const int32_t* __restrict__ w, int n_kv, const int32_t* __restrict__ cu, int n_seqs,
+                                const int32_t* __restrict__ base, int C, const float* __restrict__ edges,
+                                const int32_t* __restrict__ D, int k, int32_t* __restrict__ surv_cnt,
+                                int32_t* __restrict__ surv_pos) {
+  __shared__ float ex[NBIN - 1], ev[NBIN - 1];
+  __shared__ int32_t wsum[32];
+  const int c = blockIdx.x, g = blockIdx.y, nsig = 1 + n_kv;
+  const int total = base[n_seqs];
+  if (c >= total) return;
+  const int s = find_seq(base, n_seqs, c);
+  if (threadIdx.x < NBIN - 1) {
+    ex[threadIdx.x] = edges[((int64_t)s * nsig + 0) * (NBIN - 1) + threadIdx.x];
+    ev[threadIdx.x] = edges[((int64_t)s * nsig + 1 + g) * (NBIN - 1) + threadIdx.x];
+  }
+  __syncthreads();
+  const int start = cu[s];
+  const int p0 = (c - base[s]) * C;
+  const int p1 = min(cu[s + 1] - start, p0 + C);
+  const int32_t* Dc = D + ((int64_t)c * n_kv + g) * NCELL;
+  int32_t* outp = surv_pos + ((int64_t)c * n_kv + g) * C;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int carry = 0;
+  for (int q0 = p0; q0 < p1; q0 += blockDim.x) {
+    const int p = q0 + threadIdx.x;
+    int keep = 0;
+    if (p < p1) {
+      const int64_t t = start + p;
+      if (p >= w[t]) {
+        const int a = bin_of(vn[t * n_kv + g], ev), b = bin_of(xn[t], ex);
+        const int dom = (a == NBIN - 1 || b == NBIN - 1) ? 0 : Dc[(a + 1) * NBIN + (b + 1)];
+        keep = dom < k;
+      }
+    }
+    const unsigned ball = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) wsum[wid] = __popc(ball);
+    __syncthreads();
+    int before = carry;
+    for (int j = 0; j < wid; ++j) before += wsum[j];
+    before += __popc(ball & ((1u << lane) - 1));
+    if (keep) outp[before] = p;
+    int tot = 0;
+    for (int j = 0; j < nw; ++j) tot += wsum[j];
+    carry += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) surv_cnt[(int64_t)c * n_kv + g] = carry;
+}
+
+// per (block set, head): exact scores of the surviving candidates of earlier chunks
+__global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
+    const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w,
+    const float* __restrict__ alpha, const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base,
+    int C, int n_heads, int n_kv, int k, const double2* __restrict__ stats, const int32_t* __restrict__ surv_cnt,
+    const int32_t* __restrict__ surv_pos, int32_t* __restrict__ lmk_out) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
+  __shared__ TopkSmem sm;
+  __shared__ int32_t sel[MAX_K];
+  __shared__ int32_t offs[1025];
+  __shared__ int32_t wsum[32];
+  const int c = blockIdx.x, h = blockIdx.y;
+  const int total = base[n_seqs];
+  if (c >= total) return;
+  int32_t* out = lmk_out + ((int64_t)h * total + c) * k;  // [H, n_sets, k], n_sets = total
+  const int s = find_seq(base, n_seqs, c);
+  const int b = c - base[s];
+  const int n = b * C;
+  if (n < 2) {
+    for (int j = threadIdx.x; j < k; j += blockDim.x) out[j] = -1;
+    return;
+  }
+  const int nsig = 1 + n_kv, rep = n_heads / n_kv, g = h / rep;
+  const int start = cu[s];
+  const double2 stx = stats[(int64_t)c * nsig + 0];
+  const double2 stv = stats[(int64_t)c * nsig + 1 + g];
+  const float a = alpha[h];
+  const bool pruned = (a >= 0.0f && a <= 1.0f) && b <= 1024;
+  auto score_key = [&](int p) -> uint64_t {
+    const int64_t t = start + p;
+    if (p >= n || p < w[t]) return 0ull;
+    const float zx = __double2float_rn(__ddiv_rn(__dsub_rn((double)xn[t], stx.x), stx.y));
+    const float zv = __double2float_rn(__ddiv_rn(__dsub_rn((double)vn[t * n_kv + g], stv.x), stv.y));
+    const float sc = __fadd_rn(__fmul_rn(a, zv), __fmul_rn(__fsub_rn(1.0f, a), zx));
+    return make_key(sc, p);
+  };
+  if (!pruned) {
+    // every uncovered position of the prefix is a candidate
+    if (n <= KEY_CAP) {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) keys[i] = score_key(i);
+      __syncthreads();
+      block_topk_positions([&](int i) { return keys[i]; }, n, k, sm, sel, out);
+    } else {
+      block_topk_positions(score_key, n, k, sm, sel, out);
+    }
+    return;
+  }
+  // offsets of the survivor lists of chunks 0..b-1 of this sequence (b <= 1024)
+  const int c0 = base[s];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int carry = 0;
+  for (int j0 = 0; j0 < b; j0 += blockDim.x) {
+    const int j = j0 + threadIdx.x;
+    const int v = j < b ? surv_cnt[(int64_t)(c0 + j) * n_kv + g] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[wid] = x;
+    __syncthreads();
+    int before = carry;
+    for (int q = 0; q < wid; ++q) before += wsum[q];
+    if (j < b) offs[j] = before + x - v;
+    int tot = 0;
+    for (int q = 0; q < (int)(blockDim.x >> 5); ++q) tot += wsum[q];
+    carry += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) offs[b] = carry;
+  __syncthreads();
+  const int N = offs[b];
+  auto cand_pos = [&](int i) -> int {
+    int lo = 0, hi = b;  // offs[lo] <= i < offs[lo+1]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (offs[mid] <= i) lo = mid;
+      else hi = mid;
+    }
+    return surv_pos[((int64_t)(c0 + lo) * n_kv + g) * C + (i - offs[lo])];
+  };
+  if (N <= KEY_CAP) {
+    for (int i = threadIdx.x; i < N; i += blockDim.x) keys[i] = score_key(cand_pos(i));
+    __syncthreads();
+    block_topk_positions([&](int i) { return keys[i]; }, N, k, sm, sel, out);
+  } else {
+    block_topk_positions([&](int i) { return score_key(cand_pos(i)); }, N, k, sm, sel, out);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+struct SelectLayout {
+  size_t base_off, part_off, gstats_off, gbase_off, cand_off, stats_off, edges_off, G_off, cnt_off, pos_off, total;
+  int max_chunks, max_gchunks, nsig;
+};
+
+static SelectLayout select_layout(int mode, int64_t T, int n_seqs, int n_heads, int n_kv, int k, int block) {
+  SelectLayout L{};
+  const int C = mode == DSALT_SELECT_GLOBAL ? STAT_CHUNK : block;
+  L.nsig = 1 + n_kv;
+  L.max_chunks = (int)(T / C) + n_seqs + 1;
+  L.max_gchunks = (int)(T / GCHUNK) + n_seqs + 1;
+  size_t off = 0;
+  L.base_off = off;
+  off = align256(off + sizeof(int32_t) * (n_seqs + 1));
+  L.gbase_off = off;
+  off = align256(off + sizeof(int32_t) * (n_seqs + 1));
+  L.part_off = off;
+  off = align256(off + sizeof(Partial) * (size_t)L.max_chunks * L.nsig);
+  if (mode == DSALT_SELECT_GLOBAL) {
+    L.gstats_off = off;
+    off = align256(off + sizeof(float) * 2 * L.nsig);
+    L.cand_off = off;
+    off = align256(off + sizeof(uint64_t) * (size_t)n_heads * L.max_gchunks * k);
+  } else {
+    L.stats_off = off;
+    off = align256(off + sizeof(double2) * (size_t)L.max_chunks * L.nsig);
+    L.edges_off = off;
+    off = align256(off + sizeof(float) * (size_t)n_seqs * L.nsig * (NBIN - 1));
+    L.G_off = off;
+    off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv * NCELL);
+    L.cnt_off = off;
+    off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv);
+    L.pos_off = off;
+    off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv * C);
+  }
+  L.total = off;
+  return L;
+}
+
+size_t select_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv, int k,
+                              int block) {
+  (void)max_seqlen;
+  if (T < 0 || n_seqs < 1 || n_heads < 1 || n_kv < 1 || k < 0) return 0;
+  if (mode == DSALT_SELECT_BLOCK_CAUSAL && block <= 0) return 0;
+  return select_layout(mode, T, n_seqs, n_heads, n_kv, k, block).total;
+}
+
+static int upload_bin_table() {
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && done[dev]) return DSALT_OK;
+  float t[NBIN - 1];
+  const int nlow = NBIN / 4;  // 8 thresholds in [-1, 1.5], 23 in [1.6, 4.5]
+  for (int i = 0; i < nlow; ++i) t[i] = -1.0f + 2.5f * i / (nlow - 1);
+  const int nhigh = NBIN - 1 - nlow;
+  for (int i = 0; i < nhigh; ++i) t[nlow + i] = 1.6f + 2.9f * i / (nhigh - 1);
+  int rc = check_cuda(cudaMemcpyToSymbol(c_bin_t, t, sizeof(t)), "bin table upload");
+  if (rc == DSALT_OK && dev < 64) done[dev] = true;
+  return rc;
+}
+
+int select_set_up_attributes();
+
+int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                  const int32_t* cu, int n_seqs, int64_t T, int max_seqlen, int n_heads, int n_kv, int k, int block,
+                  int32_t* lmk_out, float* zx_out, float* zv_out, void* workspace, size_t ws_bytes,
+                  cudaStream_t stream) {
+  if (mode != DSALT_SELECT_GLOBAL && mode != DSALT_SELECT_BLOCK_CAUSAL) return fail(DSALT_ERR_INVALID, "select: mode");
+  if (n_seqs < 1 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || T < 0 || k < 0)
+    return fail(DSALT_ERR_INVALID, "select: bad sizes");
+  if (k > MAX_K) return fail(DSALT_ERR_UNSUPPORTED, "select: k=%d above %d", k, MAX_K);
+  if (T > 0x7fffff00LL) return fail(DSALT_ERR_UNSUPPORTED, "select: T too large");
+  if (mode == DSALT_SELECT_BLOCK_CAUSAL && (block < 32 || block > 1024 || block % 32))
+    return fail(DSALT_ERR_UNSUPPORTED, "select: block must be a multiple of 32 in [32, 1024]");
+  if (k == 0 || T == 0) return DSALT_OK;
+  if (!xnorm || !vnorm || !w || !alpha || !cu || !lmk_out || !workspace)
+    return fail(DSALT_ERR_INVALID, "select: null pointer");
+  const SelectLayout L = select_layout(mode, T, n_seqs, n_heads, n_kv, k, block);
+  {
+    int arc = select_set_up_attributes();  // per-device function attributes; cheap to repeat
+    if (arc) return arc;
+  }
+  if (ws_bytes < L.total) return fail(DSALT_ERR_WORKSPACE, "select: workspace %zu < %zu", ws_bytes, L.total);
+  char* ws = reinterpret_cast<char*>(workspace);
+  int32_t* cbase = reinterpret_cast<int32_t*>(ws + L.base_off);
+  Partial* part = reinterpret_cast<Partial*>(ws + L.part_off);
+  const int C = mode == DSALT_SELECT_GLOBAL ? STAT_CHUNK : block;
+  const int nsig = L.nsig;
+  chunk_table_kernel<<<1, 1024, 0, stream>>>(cu, n_seqs, C, cbase);
+  chunk_sums_kernel<<<dim3(L.max_chunks, nsig), 256, 0, stream>>>(xnorm, vnorm, n_kv, cu, n_seqs, cbase, C, part);
+  if (mode == DSALT_SELECT_GLOBAL) {
+    float* gstats = reinterpret_cast<float*>(ws + L.gstats_off);
+    int32_t* gbase = reinterpret_cast<int32_t*>(ws + L.gbase_off);
+    uint64_t* cand = reinterpret_cast<uint64_t*>(ws + L.cand_off);
+    global_stats_kernel<<<nsig, 256, 0, stream>>>(part, L.max_chunks, nsig, T, gstats);
+    chunk_table_kernel<<<1, 1024, 0, stream>>>(cu, n_seqs, GCHUNK, gbase);
+    const size_t sm1 = sizeof(uint64_t) * GCHUNK;
+    global_phase1_kernel<<<dim3(L.max_gchunks, n_heads), SEL_THREADS, sm1, stream>>>(
+        xnorm, vnorm, w, alpha, gstats, cu, n_seqs, gbase, n_heads, n_kv, k, cand, zx_out, zv_out);
+    const size_t sm2 = sizeof(uint64_t) * KEY_CAP;
+    global_phase2_kernel<<<dim3(n_seqs, n_heads), SEL_THREADS, sm2, stream>>>(cand, L.max_gchunks, gbase, n_seqs, k,
+                                                                                lmk_out);
+  } else {
+    int rc = upload_bin_table();
+    if (rc) return rc;
+    double2* stats = reinterpret_cast<double2*>(ws + L.stats_off);
+    float* edges = reinterpret_cast<float*>(ws + L.edges_off);
+    int32_t* G = reinterpret_cast<int32_t*>(ws + L.G_off);
+    int32_t* cnt = reinterpret_cast<int32_t*>(ws + L.cnt_off);
+    int32_t* pos = reinterpret_cast<int32_t*>(ws + L.pos_off);
+    block_stats_kernel<<<dim3(n_seqs, nsig), 256, 0, stream>>>(part, cu, n_seqs, cbase, nsig, C, stats, edges);
+    dominance_hist_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
+                                                                        edges, G);
+    dominance_scan_kernel<<<dim3(n_seqs * n_kv, NCELL / 256), 256, 0, stream>>>(G, cbase, n_kv);
+    survivor_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges,
+                                                                  G, k, cnt, pos);
+    const size_t sm3 = sizeof(uint64_t) * KEY_CAP;
+    block_select_kernel<<<dim3(L.max_chunks, n_heads), SEL_THREADS, sm3, stream>>>(
+        xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, cnt, pos, lmk_out);
+  }
+  return check_cuda(cudaGetLastError(), "select launch");
+}
+
+int select_set_up_attributes() {
+  int rc = check_cuda(cudaFuncSetAttribute(global_phase2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)(sizeof(uint64_t) * KEY_CAP)),
+                      "smem attr");
+  if (rc) return rc;
+  return check_cuda(cudaFuncSetAttribute(block_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(sizeof(uint64_t) * KEY_CAP)),
+                    "smem attr");
+}
+
+}  // namespace dsalt

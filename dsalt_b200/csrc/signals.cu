@@ -1,0 +1,198 @@
+// Per-token window width and selection signals in one pass over x and v.
+//
+// Follows dsalt/modules/dsalt_attention.py:270-284 (width: win_gate logit, sigmoid,
+// affine map, floor, clamp) and dsalt/kernels/landmark_tokens_ker.py:47,52 (the norms
+// ‖x_i‖ and ‖(x W_Vᵀ)_{i,g}‖ used by the landmark score).
+//
+// Arithmetic contract (shared with the CPU oracle):
+//  * logit: Σ x_i·g_i + b accumulated in float64 (products of two <=24-bit values are
+//    exact) and rounded once to the gate dtype;
+//  * sigmoid: 1/(1+expf(-l)) in fp32 (the expression torch's CUDA sigmoid evaluates),
+//    then every op of `n_min + σ·(n_max−n_min)` rounds to the gate dtype, floor, >= 1;
+//  * norms: sum of squares in float64 rounded once to fp32, IEEE fp32 sqrt, optionally
+//    rounded to the input dtype.
+// One warp per token; 16-byte vector loads; HBM-bound (reads x and v once).
+#include "common.cuh"
+
+namespace dsalt {
+
+template <int DT> struct Vec;
+template <> struct Vec<DSALT_BF16> {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void load(const void* p, float* out) {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(h[i]);
+      out[2 * i] = f.x;
+      out[2 * i + 1] = f.y;
+    }
+  }
+};
+template <> struct Vec<DSALT_F16> {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void load(const void* p, float* out) {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __half22float2(h[i]);
+      out[2 * i] = f.x;
+      out[2 * i + 1] = f.y;
+    }
+  }
+};
+template <> struct Vec<DSALT_F32> {
+  static constexpr int N = 4;
+  static __device__ __forceinline__ void load(const void* p, float* out) {
+    float4 u = __ldg(reinterpret_cast<const float4*>(p));
+    out[0] = u.x;
+    out[1] = u.y;
+    out[2] = u.z;
+    out[3] = u.w;
+  }
+};
+
+template <int DT> __device__ __forceinline__ const char* elem_ptr(const void* base, int64_t off) {
+  constexpr int ES = DT == DSALT_F32 ? 4 : 2;
+  return reinterpret_cast<const char*>(base) + off * ES;
+}
+
+__device__ __forceinline__ int width_from_logit(float l, int gate_dt, int n_min, int n_max) {
+  // torch: one / (one + exp(-x)) in fp32 opmath, result rounded to the tensor dtype
+  float s = 1.0f / (1.0f + expf(-l));
+  s = round_to(s, gate_dt);
+  float m = round_to(__fmul_rn(s, (float)(n_max - n_min)), gate_dt);
+  float c = round_to(__fadd_rn(m, (float)n_min), gate_dt);
+  float f = floorf(c);
+  int w = (f >= 2147483520.0f) ? 2147483520 : (int)f;  // c is finite and bounded by n_max
+  return w < 1 ? 1 : w;
+}
+
+template <int XDT, int VDT>
+__global__ void __launch_bounds__(256) token_signals_kernel(
+    const void* __restrict__ x, int64_t T, int d_model, int64_t x_stride, const void* __restrict__ gate_w,
+    const void* __restrict__ gate_b, int gate_dt, int n_min, int n_max, const void* __restrict__ v, int64_t v_stride,
+    int n_kv, int head_dim, int norm_mode, int32_t* __restrict__ w_out, float* __restrict__ xnorm_out,
+    float* __restrict__ vnorm_out, float* __restrict__ logit_out) {
+  constexpr int XN = Vec<XDT>::N;
+  constexpr int VN = Vec<VDT>::N;
+  const int lane = threadIdx.x & 31;
+  const int warps_per_block = blockDim.x >> 5;
+  const int64_t warp0 = (int64_t)blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * warps_per_block;
+  const int x_chunks = d_model / XN;
+  const int v_chunks_per_group = head_dim / VN;
+  const int v_chunks = n_kv * v_chunks_per_group;
+  const double bias = (double)load_elem(gate_b, 0, gate_dt);
+
+  for (int64_t t = warp0; t < T; t += nwarps) {
+    const char* xr = elem_ptr<XDT>(x, t * x_stride);
+    double dot = 0.0, sq = 0.0;
+    for (int c = lane; c < x_chunks; c += 32) {
+      float xv[XN];
+      Vec<XDT>::load(xr + (size_t)c * 16, xv);
+#pragma unroll
+      for (int i = 0; i < XN; ++i) {
+        const float g = load_elem(gate_w, (int64_t)c * XN + i, gate_dt);
+        const float xg = round_to(xv[i], gate_dt);
+        dot = __fma_rn((double)xg, (double)g, dot);
+        sq = __fma_rn((double)xv[i], (double)xv[i], sq);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    }
+    if (lane == 0) {
+      const float logit = f64_to(dot + bias, gate_dt);
+      w_out[t] = width_from_logit(logit, gate_dt, n_min, n_max);
+      if (logit_out) logit_out[t] = logit;
+      float xn = sqrtf(__double2float_rn(sq));
+      if (norm_mode == DSALT_NORM_INPUT) xn = round_to(xn, XDT);
+      xnorm_out[t] = xn;
+    }
+    // value norms: head_dim/VN consecutive chunks form one kv group
+    const char* vr = elem_ptr<VDT>(v, t * v_stride);
+    if (v_chunks_per_group <= 32) {
+      for (int base = 0; base < v_chunks; base += 32) {
+        const int c = base + lane;
+        double s = 0.0;
+        if (c < v_chunks) {
+          float vv[VN];
+          Vec<VDT>::load(vr + (size_t)c * 16, vv);
+#pragma unroll
+          for (int i = 0; i < VN; ++i) s = __fma_rn((double)vv[i], (double)vv[i], s);
+        }
+        for (int o = v_chunks_per_group >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (c < v_chunks && (c % v_chunks_per_group) == 0) {
+          float vn = sqrtf(__double2float_rn(s));
+          if (norm_mode == DSALT_NORM_INPUT) vn = round_to(vn, VDT);
+          vnorm_out[t * n_kv + c / v_chunks_per_group] = vn;
+        }
+      }
+    } else {
+      for (int g = 0; g < n_kv; ++g) {
+        double s = 0.0;
+        for (int c = lane; c < v_chunks_per_group; c += 32) {
+          float vv[VN];
+          Vec<VDT>::load(vr + ((size_t)g * v_chunks_per_group + c) * 16, vv);
+#pragma unroll
+          for (int i = 0; i < VN; ++i) s = __fma_rn((double)vv[i], (double)vv[i], s);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) {
+          float vn = sqrtf(__double2float_rn(s));
+          if (norm_mode == DSALT_NORM_INPUT) vn = round_to(vn, VDT);
+          vnorm_out[t * n_kv + g] = vn;
+        }
+      }
+    }
+  }
+}
+
+static bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+
+int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride, const void* gate_w,
+                         const void* gate_b, int gate_dtype, int n_min, int n_max, const void* v, int v_dtype,
+                         int64_t v_stride, int n_kv, int head_dim, int norm_mode, int32_t* w_out, float* xnorm_out,
+                         float* vnorm_out, float* logit_out, cudaStream_t stream) {
+  if (T < 0 || d_model <= 0 || n_kv <= 0 || head_dim <= 0) return fail(DSALT_ERR_INVALID, "token_signals: bad sizes");
+  if (T == 0) return DSALT_OK;
+  if (!x || !gate_w || !gate_b || !v || !w_out || !xnorm_out || !vnorm_out)
+    return fail(DSALT_ERR_INVALID, "token_signals: null pointer");
+  for (int dt : {x_dtype, v_dtype, gate_dtype})
+    if (dt != DSALT_F32 && dt != DSALT_BF16 && dt != DSALT_F16) return fail(DSALT_ERR_INVALID, "token_signals: dtype");
+  if (norm_mode != DSALT_NORM_F32 && norm_mode != DSALT_NORM_INPUT)
+    return fail(DSALT_ERR_INVALID, "token_signals: norm_mode");
+  if (n_max < n_min) return fail(DSALT_ERR_INVALID, "token_signals: n_max < n_min");
+  const int xes = x_dtype == DSALT_F32 ? 4 : 2, ves = v_dtype == DSALT_F32 ? 4 : 2;
+  const int xvec = 16 / xes, vvec = 16 / ves;
+  if (d_model % xvec || head_dim % vvec || !is_pow2(head_dim / vvec))
+    return fail(DSALT_ERR_UNSUPPORTED, "token_signals: d_model must be a multiple of %d and head_dim/%d a power of two",
+                xvec, vvec);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(v)) & 15 || (x_stride * xes) % 16 ||
+      (v_stride * ves) % 16)
+    return fail(DSALT_ERR_INVALID, "token_signals: x/v rows must be 16-byte aligned");
+  if (x_stride < d_model || v_stride < (int64_t)n_kv * head_dim) return fail(DSALT_ERR_INVALID, "token_signals: stride");
+  const int threads = 256;
+  int64_t blocks = (T + 7) / 8;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+#define DSALT_SIG_LAUNCH(XD, VD)                                                                                   \
+  token_signals_kernel<XD, VD><<<(unsigned)blocks, threads, 0, stream>>>(                                          \
+      x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_stride, n_kv, head_dim, norm_mode, \
+      w_out, xnorm_out, vnorm_out, logit_out)
+  if (x_dtype == DSALT_BF16 && v_dtype == DSALT_BF16) DSALT_SIG_LAUNCH(DSALT_BF16, DSALT_BF16);
+  else if (x_dtype == DSALT_F16 && v_dtype == DSALT_F16) DSALT_SIG_LAUNCH(DSALT_F16, DSALT_F16);
+  else if (x_dtype == DSALT_F32 && v_dtype == DSALT_F32) DSALT_SIG_LAUNCH(DSALT_F32, DSALT_F32);
+  else if (x_dtype == DSALT_F32 && v_dtype == DSALT_BF16) DSALT_SIG_LAUNCH(DSALT_F32, DSALT_BF16);
+  else if (x_dtype == DSALT_F32 && v_dtype == DSALT_F16) DSALT_SIG_LAUNCH(DSALT_F32, DSALT_F16);
+  else return fail(DSALT_ERR_UNSUPPORTED, "token_signals: x/v dtype combination");
+#undef DSALT_SIG_LAUNCH
+  return check_cuda(cudaGetLastError(), "token_signals launch");
+}
+
+}  // namespace dsalt

@@ -1,0 +1,125 @@
+"""``DSALTAttention`` with the reference's constructor, parameters and forward signature
+(``dsalt/modules/dsalt_attention.py:147-369``), whose packed inference path runs on the
+B200 kernels of this package.
+
+Same state-dict keys (``q_proj``, ``k_proj``, ``v_proj``, ``out_proj``, ``win_gate``,
+``alpha_w``), same RoPE cache and half-split rotation, same ``(out, aux)`` return. The
+packed path (``cu_seqlens`` given) replaces ``_packed``'s inference branch
+(``:610-641``): widths, landmark selection and the sparse attention run in CUDA, the
+projections, RoPE and ``out_proj`` stay library GEMMs/elementwise ops. Grouped kv heads
+are indexed by the kernels instead of being repeated (``_repeat_kv``, ``:254-268``).
+
+``selection="block_causal"`` selects per ``block`` queries from earlier positions only,
+as ``results/causal_landmark_check.py``'s ``"block"`` mode does.
+
+Out of scope (raise): the training path, the batched ``[B, T, d]`` path, and the dense
+``_last_P`` rebuild (``:636-704``); ``_collect_last_P`` defaults to False here.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+
+
+def build_rope_cache(seq_len, head_dim, device, dtype=torch.float32, base=10000.0, scale=1.0):
+    """RoPE ``(cos, sin)`` ``[seq_len, head_dim]`` (same numbers as the reference's
+    ``build_rope_cache``, ``dsalt/kernels/window_utils.py:91-106``)."""
+    theta = 1.0 / (base ** (torch.arange(0, head_dim, 2, device=device, dtype=dtype) / head_dim))
+    positions = torch.arange(seq_len, device=device, dtype=dtype) / scale
+    emb = torch.cat([torch.outer(positions, theta)] * 2, dim=-1)
+    return emb.cos(), emb.sin()
+
+
+def apply_rotary_emb(q, k, cos, sin):
+    """Half-split rotary embedding, op for op as the reference's ``apply_rotary_emb``
+    (``dsalt/kernels/window_utils.py:73-88``)."""
+    half = q.shape[-1] // 2
+
+    def rot(x):
+        return torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+
+    return q * cos + rot(q) * sin, k * cos + rot(k) * sin
+
+
+class DSALTAttention(nn.Module):
+    def __init__(self, d_model, n_heads, n_min, n_max, k_lmk, max_seq_len, dropout=0.0, yarn_scale=1.0,
+                 layer_idx=0, n_kv_heads=None, qkv_bias=False, rope_base=10000.0, selection="global", block=512):
+        super().__init__()
+        assert d_model % n_heads == 0
+        if selection not in ("global", "block_causal"):
+            raise ValueError("selection must be 'global' or 'block_causal'")
+        self.d_model = d_model
+        self.n_heads = n_heads
+        self.head_dim = d_model // n_heads
+        self.n_kv_heads = n_kv_heads if n_kv_heads is not None else n_heads
+        assert n_heads % self.n_kv_heads == 0, "n_heads must be a multiple of n_kv_heads"
+        self.n_rep = n_heads // self.n_kv_heads
+        self.kv_dim = self.n_kv_heads * self.head_dim
+        self.n_min, self.n_max, self.k_lmk = n_min, n_max, k_lmk
+        self.max_seq_len = max_seq_len
+        self.dropout = dropout
+        self.yarn_scale = yarn_scale
+        self.rope_base = rope_base
+        self.layer_idx = layer_idx
+        self.selection = selection
+        self.block = block
+        self.q_proj = nn.Linear(d_model, d_model, bias=qkv_bias)
+        self.k_proj = nn.Linear(d_model, self.kv_dim, bias=qkv_bias)
+        self.v_proj = nn.Linear(d_model, self.kv_dim, bias=qkv_bias)
+        self.out_proj = nn.Linear(d_model, d_model, bias=False)
+        self.win_gate = nn.Linear(d_model, 1, bias=True)
+        self.alpha_w = nn.Parameter(torch.full((n_heads,), math.log(0.6 / 0.4)))
+        self.tau_win, self.tau_lmk, self.win_edge = 1.0, 2.0, 4
+        self._last_P = None
+        self._collect_last_P = False
+        cos, sin = build_rope_cache(max_seq_len, self.head_dim, torch.device("cpu"), base=rope_base, scale=yarn_scale)
+        self.register_buffer("rope_cos", cos, persistent=False)
+        self.register_buffer("rope_sin", sin, persistent=False)
+
+    def _alpha(self):
+        return torch.sigmoid(self.alpha_w)
+
+    def forward(self, x, cu_seqlens=None, max_seqlen=None, rope_cs=None, cu_list=None):
+        if cu_seqlens is None:
+            raise NotImplementedError("dsalt_b200 implements the packed path; pass cu_seqlens")
+        if self.training:
+            raise NotImplementedError("dsalt_b200 implements the inference forward; call .eval()")
+        if self._collect_last_P:
+            raise NotImplementedError("the dense _last_P rebuild is not part of dsalt_b200")
+        return self._packed(x, cu_seqlens, x.shape[0], x.device, rope_cs, cu_list)
+
+    @torch.no_grad()
+    def _packed(self, x, cu_seqlens, total_len, device, rope_cs=None, cu_list=None):
+        T, H, Hkv, D = total_len, self.n_heads, self.n_kv_heads, self.head_dim
+        cu_h = ops._host_cu(cu_seqlens, cu_list)
+        q = self.q_proj(x).view(T, H, D)
+        k = self.k_proj(x).view(T, Hkv, D)
+        v = self.v_proj(x).view(T, Hkv, D)
+        if rope_cs is None:
+            pos = torch.cat([torch.arange(cu_h[i + 1] - cu_h[i], device=device) for i in range(len(cu_h) - 1)])
+            cos, sin = self.rope_cos.to(device)[pos], self.rope_sin.to(device)[pos]
+        else:
+            cos, sin = rope_cs
+        cos, sin = cos.to(q.dtype), sin.to(q.dtype)
+        q, k = apply_rotary_emb(q, k, cos.unsqueeze(1), sin.unsqueeze(1))
+        amp = torch.is_autocast_enabled("cuda") if x.is_cuda else False
+        gdt = torch.get_autocast_dtype("cuda") if amp else x.dtype
+        gw = self.win_gate.weight.to(gdt)
+        gb = self.win_gate.bias.to(gdt)
+        # value norms use x·W_Vᵀ, which is the v_proj output when there is no bias
+        vs = v if self.v_proj.bias is None else F.linear(x, self.v_proj.weight.to(v.dtype))
+        norm_round = (x.dtype != torch.float32) and not amp
+        w, xn, vn = ops.window_signals(x, gw, gb, self.n_min, self.n_max, vs, D, norm_round)
+        alpha = self._alpha().detach().float()
+        mode = "global" if self.selection == "global" else "block_causal"
+        lmk = ops.select_landmarks(xn, vn, w, alpha, cu_seqlens, self.k_lmk, H, mode, self.block, cu_list=cu_h)
+        out = ops.dsalt_attention(q.contiguous(), k.contiguous(), v.contiguous(), lmk, None, w, cu_seqlens,
+                                  lmk_block=0 if mode == "global" else self.block, out_dtype=q.dtype, cu_list=cu_h)
+        self._last_P = None
+        aux = torch.zeros((), device=x.device, dtype=x.dtype)
+        return self.out_proj(out.view(T, self.d_model).to(self.out_proj.weight.dtype)), aux

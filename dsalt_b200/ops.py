@@ -1,0 +1,264 @@
+"""Torch-facing operators over the C ABI, mirroring the reference's functions.
+
+* :func:`window_signals`            — ``DSALTAttention._window_sizes(x, floor=True)``
+  (``dsalt/modules/dsalt_attention.py:270-284``) fused with the selection norms of
+  ``hybrid_scores_per_head`` (``dsalt/kernels/landmark_tokens_ker.py:47,52``)
+* :func:`compute_landmark_indices`  — ``_compute_landmark_indices``
+  (``dsalt/kernels/selectors.py:75-134``), same arguments and return values
+* :func:`select_landmarks`          — whole-sequence or block-causal selection from the
+  signals (block-causal: ``results/causal_landmark_check.py:82-113``)
+* :func:`dsalt_attention`           — ``dsalt_triton_attention``
+  (``dsalt/kernels/dsalt_triton_attn.py:337-349``), same arguments; returns fp32 like the
+  reference unless ``out_dtype`` is given
+* :func:`core_forward`              — widths + selection + attention in one C call.
+
+Tensors must be CUDA tensors; every call launches on the current stream. There is no
+CPU path: a CPU tensor raises.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.F32, torch.bfloat16: L.BF16, torch.float16: L.F16}
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}") from None
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("dsalt_b200 operators need CUDA tensors (no CPU path)")
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _host_cu(cu_seqlens: torch.Tensor, cu_list):
+    if cu_list is not None:
+        return [int(c) for c in cu_list]
+    return [int(c) for c in cu_seqlens.detach().to("cpu").tolist()]
+
+
+def _cu_i32(cu_seqlens: torch.Tensor) -> torch.Tensor:
+    cu = cu_seqlens if cu_seqlens.dtype == torch.int32 else cu_seqlens.to(torch.int32)
+    return cu.contiguous()
+
+
+def n_block_sets(cu_list, block: int) -> int:
+    return sum((cu_list[i + 1] - cu_list[i] + block - 1) // block for i in range(len(cu_list) - 1))
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+# --------------------------------------------------------------------------- widths
+def window_signals(x, gate_weight, gate_bias, n_min: int, n_max: int, v, head_dim: int, norm_round: bool = False,
+                   return_logit: bool = False):
+    """Widths ``w [T] int32``, ``‖x‖ [T] fp32`` and value norms ``[T, n_kv] fp32``.
+
+    ``gate_weight``/``gate_bias`` are ``win_gate``'s parameters already in the dtype the
+    logit is computed in (the autocast dtype under autocast). ``v`` is ``x·W_Vᵀ``
+    (``[T, n_kv·head_dim]``, or a ``[T, n_kv, head_dim]`` view). ``norm_round`` rounds the
+    norms to the input dtype (a half-precision ``norm`` outside autocast).
+    """
+    _cuda(x, gate_weight, gate_bias, v)
+    T, dm = x.shape
+    v2 = v.reshape(T, -1)
+    if v2.stride(1) != 1:
+        v2 = v2.contiguous()
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    n_kv = v2.shape[1] // head_dim
+    gw = gate_weight.reshape(-1).contiguous()
+    gb = gate_bias.reshape(-1).to(gw.dtype).contiguous()
+    w = torch.empty(T, dtype=torch.int32, device=x.device)
+    xn = torch.empty(T, dtype=torch.float32, device=x.device)
+    vn = torch.empty(T, n_kv, dtype=torch.float32, device=x.device)
+    lg = torch.empty(T, dtype=torch.float32, device=x.device) if return_logit else None
+    L.call("dsalt_token_signals", _ptr(x), _dt(x), T, dm, x.stride(0), _ptr(gw), _ptr(gb), _dt(gw), int(n_min),
+           int(n_max), _ptr(v2), _dt(v2), v2.stride(0), n_kv, int(head_dim),
+           L.NORM_INPUT if norm_round else L.NORM_F32, _ptr(w), _ptr(xn), _ptr(vn), _ptr(lg), _stream())
+    if return_logit:
+        return w, xn, vn, lg
+    return w, xn, vn
+
+
+# --------------------------------------------------------------------------- selection
+def select_landmarks(xnorm, vnorm, w, alpha, cu_seqlens, k_lmk: int, n_heads: int, mode: str = "global",
+                     block: int = 512, cu_list=None, return_z: bool = False):
+    """Landmark sets ``[H, n_sets, k] int32`` (ascending positions within the sequence,
+    ``-1`` padded). ``mode`` is ``"global"`` (one set per sequence) or ``"block_causal"``
+    (one set per ``block`` queries, drawn from earlier positions)."""
+    _cuda(xnorm, vnorm, w, alpha, cu_seqlens)
+    cu_h = _host_cu(cu_seqlens, cu_list)
+    S = len(cu_h) - 1
+    T = int(xnorm.shape[0])
+    n_kv = int(vnorm.shape[1])
+    maxL = max([cu_h[i + 1] - cu_h[i] for i in range(S)] + [0])
+    m = L.SELECT_GLOBAL if mode == "global" else L.SELECT_BLOCK_CAUSAL
+    n_sets = S if m == L.SELECT_GLOBAL else n_block_sets(cu_h, block)
+    dev = xnorm.device
+    lmk = torch.empty(n_heads, n_sets, k_lmk, dtype=torch.int32, device=dev)
+    zx = torch.empty(T, dtype=torch.float32, device=dev) if (return_z and m == L.SELECT_GLOBAL) else None
+    zv = torch.empty(T, n_kv, dtype=torch.float32, device=dev) if (return_z and m == L.SELECT_GLOBAL) else None
+    if T == 0 or k_lmk == 0:
+        lmk.fill_(-1)
+        return (lmk, zx, zv) if return_z else lmk
+    ws_n = L.query("dsalt_select_workspace_bytes", m, T, S, maxL, n_heads, n_kv, k_lmk, block)
+    ws = _workspace(ws_n, dev)
+    a = alpha.float().contiguous()
+    L.call("dsalt_select_landmarks", m, _ptr(xnorm.contiguous()), _ptr(vnorm.contiguous()),
+           _ptr(w.to(torch.int32).contiguous()), _ptr(a), _ptr(_cu_i32(cu_seqlens)), S, T, maxL, n_heads, n_kv,
+           k_lmk, block, _ptr(lmk), _ptr(zx), _ptr(zv), _ptr(ws), ws.numel(), _stream())
+    return (lmk, zx, zv) if return_z else lmk
+
+
+def compute_landmark_indices(x, W_V, alpha, w_sizes, cu_seqlens, k_lmk, n_min, total_len, cu_list=None,
+                             head_dim=None, *, v=None, norm_round=None):
+    """Drop-in for ``_compute_landmark_indices`` (``dsalt/kernels/selectors.py:75-86``).
+
+    Returns ``(lmk [H, S, k] int64, z_x [T], z_v [T, H])``. The value norms use ``v`` if
+    given (the ``v_proj`` output, equal to ``x @ W_Vᵀ`` without bias), else ``x @ W_Vᵀ``
+    computed here with a library GEMM. ``norm_round`` defaults to the reference's dtype
+    behaviour: fp32 norms under CUDA autocast or for fp32 inputs, input-dtype norms for a
+    half-precision ``x`` outside autocast.
+    """
+    del n_min, total_len
+    H = int(alpha.shape[0])
+    dh = head_dim if head_dim is not None else W_V.shape[0] // H
+    if v is None:
+        v = x @ W_V.T
+    if norm_round is None:
+        norm_round = x.dtype != torch.float32 and not torch.is_autocast_enabled("cuda")
+    w = w_sizes.to(torch.int32)
+    n_kv = v.reshape(x.shape[0], -1).shape[1] // dh
+    vn = _norms_only(x, v, dh, norm_round)
+    xn = vn[0]
+    lmk, zx, zv = select_landmarks(xn, vn[1], w, alpha, cu_seqlens, int(k_lmk), H, "global", cu_list=cu_list,
+                                   return_z=True)
+    if n_kv != H:
+        zv = zv.repeat_interleave(H // n_kv, dim=1)
+    return lmk.long(), zx, zv
+
+
+def _norms_only(x, v, head_dim, norm_round):
+    T, dm = x.shape
+    gw = torch.zeros(dm, dtype=x.dtype, device=x.device)
+    gb = torch.zeros(1, dtype=x.dtype, device=x.device)
+    _, xn, vn = window_signals(x, gw, gb, 1, 1, v, head_dim, norm_round)
+    return xn, vn
+
+
+# --------------------------------------------------------------------------- attention
+def dsalt_attention(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, *, lmk_block: int = 0, out_dtype=None,
+                    cu_list=None, return_lse: bool = False):
+    """Drop-in for ``dsalt_triton_attention(q, k, v, lmk_indices, lmk_bias, w_sizes,
+    cu_seqlens)`` (``dsalt/kernels/dsalt_triton_attn.py:337-349``).
+
+    ``q [T, H, D]``; ``k, v [T, H or H_kv, D]`` (grouped heads are indexed, not
+    repeated); ``lmk_indices [H, n_sets, k]`` positions within the sequence (any order,
+    ``-1`` = none); ``lmk_block`` > 0 gives one set per ``lmk_block`` queries. The result
+    is fp32 like the reference (values rounded to the input dtype when the input is
+    bf16/fp16, as the reference stores its output before widening); pass ``out_dtype``
+    to skip the widening. fp32 inputs run in fp32 on CUDA cores.
+    """
+    _cuda(q, k, v, lmk_indices, w_sizes, cu_seqlens)
+    T, H, D = q.shape
+    if k.shape[-1] != D or v.shape != k.shape:
+        raise ValueError("k and v must be [T, H_kv, D] with the head_dim of q")
+    n_kv = k.shape[1]
+    dt = q.dtype
+    if k.dtype != dt or v.dtype != dt:
+        raise TypeError("q, k, v must share a dtype")
+    qc = q if (q.stride(2) == 1 and q.stride(1) == D) else q.contiguous()
+    kc = k.contiguous() if not (k.stride(2) == 1 and k.stride(1) == D) else k
+    vc = v.contiguous() if not (v.stride(2) == 1 and v.stride(1) == D) else v
+    if kc.stride(0) != vc.stride(0):
+        kc, vc = kc.contiguous(), vc.contiguous()
+    cu_h = _host_cu(cu_seqlens, cu_list)
+    S = len(cu_h) - 1
+    maxL = max([cu_h[i + 1] - cu_h[i] for i in range(S)] + [0])
+    lmk = lmk_indices.to(torch.int32).contiguous()
+    kl = int(lmk.shape[-1])
+    bias = None if lmk_bias is None else lmk_bias.to(torch.float32).contiguous()
+    odt = out_dtype if out_dtype is not None else (dt if dt != torch.float32 else torch.float32)
+    out = torch.empty(T, H, D, dtype=odt, device=q.device)
+    lse = torch.empty(T, H, dtype=torch.float32, device=q.device) if return_lse else None
+    ws_n = L.query("dsalt_attention_workspace_bytes", T, S, H, kl, int(lmk_block))
+    ws = _workspace(ws_n, q.device)
+    L.call("dsalt_attention_fwd", _ptr(qc), _ptr(kc), _ptr(vc), _dt(qc), T, H, n_kv, D, qc.stride(0), kc.stride(0),
+           _ptr(w_sizes.to(torch.int32).contiguous()), _ptr(lmk), _ptr(bias), kl, int(lmk_block),
+           _ptr(_cu_i32(cu_seqlens)), S, maxL, _ptr(out), _dt(out), _ptr(lse), _ptr(ws), ws.numel(), _stream())
+    if out_dtype is None:
+        out = out.float()
+    return (out, lse) if return_lse else out
+
+
+# --------------------------------------------------------------------------- fused core
+def core_forward(x, gate_weight, gate_bias, n_min, n_max, alpha, q, k, v, k_lmk, cu_seqlens, *, mode="global",
+                 block=512, norm_round=False, out_dtype=None, cu_list=None, return_aux=False, workspace=None,
+                 out=None):
+    """Widths, selection and attention in one C call (``dsalt_core_forward``).
+
+    ``v`` ([T, n_kv, D]) is used both as attention values and for the value norms, so
+    it must equal ``x·W_Vᵀ`` (no ``v_proj`` bias). Returns the attention output
+    ``[T, H, D]`` (``out_dtype``, default the input dtype) and, with ``return_aux``, the
+    widths and landmark sets.
+    """
+    _cuda(x, gate_weight, gate_bias, alpha, q, k, v, cu_seqlens)
+    T, H, D = q.shape
+    n_kv = k.shape[1]
+    cu_h = _host_cu(cu_seqlens, cu_list)
+    S = len(cu_h) - 1
+    maxL = max([cu_h[i + 1] - cu_h[i] for i in range(S)] + [0])
+    m = L.SELECT_GLOBAL if mode == "global" else L.SELECT_BLOCK_CAUSAL
+    n_sets = S if m == L.SELECT_GLOBAL else n_block_sets(cu_h, block)
+    dev = q.device
+    gw = gate_weight.reshape(-1).contiguous()
+    gb = gate_bias.reshape(-1).to(gw.dtype).contiguous()
+    odt = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(T, H, D, dtype=odt, device=dev)
+    w = torch.empty(T, dtype=torch.int32, device=dev) if return_aux else None
+    lmk = torch.empty(H, n_sets, k_lmk, dtype=torch.int32, device=dev) if return_aux else None
+    need = L.query("dsalt_core_workspace_bytes", m, T, S, maxL, H, n_kv, D, k_lmk, block)
+    ws = workspace if (workspace is not None and workspace.numel() >= need) else _workspace(need, dev)
+    L.call("dsalt_core_forward", m, _ptr(x), _dt(x), x.shape[1], x.stride(0), _ptr(gw), _ptr(gb), _dt(gw),
+           int(n_min), int(n_max), _ptr(alpha.float().contiguous()), L.NORM_INPUT if norm_round else L.NORM_F32,
+           _ptr(q), _ptr(k), _ptr(v), _dt(q), H, n_kv, D, q.stride(0), k.stride(0), int(k_lmk), int(block),
+           _ptr(_cu_i32(cu_seqlens)), S, T, maxL, _ptr(out), _dt(out), _ptr(w), _ptr(lmk), _ptr(ws), ws.numel(),
+           _stream())
+    if return_aux:
+        return out, w, lmk
+    return out
+
+
+def core_workspace_bytes(T, n_seqs, max_seqlen, n_heads, n_kv, head_dim, k_lmk, mode="global", block=512) -> int:
+    m = L.SELECT_GLOBAL if mode == "global" else L.SELECT_BLOCK_CAUSAL
+    return L.query("dsalt_core_workspace_bytes", m, T, n_seqs, max_seqlen, n_heads, n_kv, head_dim, k_lmk, block)
+
+
+def device_status(clear: bool = True) -> int:
+    import ctypes
+    st = ctypes.c_int(0)
+    L.call("dsalt_device_status", ctypes.byref(st), 1 if clear else 0, _stream())
+    return int(st.value)
+
+
+def scale_for(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

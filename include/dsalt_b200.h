@@ -1,0 +1,137 @@
+/*
+ * dsalt_b200: B200 (sm_100a) kernels for the DSALT sparse-attention forward.
+ *
+ * C ABI: plain pointers, sizes and a CUDA stream (passed as void*). All pointers are
+ * device pointers unless stated otherwise; nothing here allocates device memory —
+ * callers pass output buffers and a workspace sized by the *_workspace_bytes queries.
+ * Every entry point returns DSALT_OK (0) or an error code and leaves a message for
+ * dsalt_last_error(). Kernels are launched asynchronously on `stream`.
+ *
+ * Each function cites the reference (LeonardoCofone/dsalt) interface it replaces.
+ */
+#ifndef DSALT_B200_H
+#define DSALT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define DSALT_F32 0
+#define DSALT_BF16 1
+#define DSALT_F16 2
+
+/* status codes */
+#define DSALT_OK 0
+#define DSALT_ERR_INVALID 1       /* bad shape, dtype, stride, alignment or pointer */
+#define DSALT_ERR_UNSUPPORTED 2   /* valid request outside what the kernels implement */
+#define DSALT_ERR_CUDA 3          /* a CUDA runtime/driver call failed */
+#define DSALT_ERR_WORKSPACE 4     /* workspace smaller than the *_workspace_bytes query */
+#define DSALT_ERR_DEVICE 5        /* a kernel gave up a bounded wait (see dsalt_device_status) */
+
+/* selection modes */
+#define DSALT_SELECT_GLOBAL 0       /* one landmark set per (head, sequence) */
+#define DSALT_SELECT_BLOCK_CAUSAL 1 /* one landmark set per (head, block of queries) */
+
+/* norm rounding of the selection signals */
+#define DSALT_NORM_F32 0   /* fp32 norms (CUDA autocast runs `norm` in fp32) */
+#define DSALT_NORM_INPUT 1 /* norms rounded to the input dtype (bf16/fp16 `norm` outside autocast) */
+
+const char* dsalt_last_error(void);
+int dsalt_version(void);
+
+/* Reads (and clears, when `clear` != 0) the device status word that kernels set when a
+ * bounded wait gives up. Synchronises `stream`. 0 = no error. */
+int dsalt_device_status(int* status_out, int clear, void* stream);
+
+/*
+ * Window widths and selection signals, one pass over x and v.
+ * Replaces DSALTAttention._window_sizes(x, floor=True)
+ *   (dsalt/modules/dsalt_attention.py:270-284, win_gate at :223)
+ * and the norms of hybrid_scores_per_head / _token_signals
+ *   (dsalt/kernels/landmark_tokens_ker.py:47,52; results/causal_landmark_check.py:68-79).
+ *
+ * x        [T, d_model] (row stride x_stride elements), dtype x_dtype
+ * gate_w   [d_model], gate_b [1]: win_gate weight/bias in gate_dtype; the logit is
+ *          computed in gate_dtype (x converted to gate_dtype first, as autocast does)
+ * v        [T, n_kv*head_dim] value projection x·W_Vᵀ (row stride v_stride), dtype v_dtype
+ * w_out    [T] int32 widths, xnorm_out [T] fp32, vnorm_out [T, n_kv] fp32
+ * logit_out [T] fp32 (nullable): the rounded win_gate logit
+ */
+int dsalt_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride,
+                        const void* gate_w, const void* gate_b, int gate_dtype, int n_min, int n_max,
+                        const void* v, int v_dtype, int64_t v_stride, int n_kv, int head_dim, int norm_mode,
+                        int32_t* w_out, float* xnorm_out, float* vnorm_out, float* logit_out, void* stream);
+
+/*
+ * Landmark selection.
+ * DSALT_SELECT_GLOBAL replaces _compute_landmark_indices
+ *   (dsalt/kernels/selectors.py:75-134) with hybrid_scores_per_head
+ *   (dsalt/kernels/landmark_tokens_ker.py:19-61): statistics over all T packed tokens,
+ *   top-k per (head, sequence) among tokens with seq_off >= w.
+ * DSALT_SELECT_BLOCK_CAUSAL replaces the per-block _select of
+ *   results/causal_landmark_check.py:82-113 (driven at :176-186): block b of each
+ *   sequence draws from positions [0, b*block) with that prefix's statistics.
+ *
+ * xnorm [T], vnorm [T, n_kv], w [T] (int32), alpha [n_heads] (sigmoid(alpha_w), fp32)
+ * cu_seqlens [n_seqs+1] int32 (device), max_seqlen: host upper bound of sequence lengths
+ * lmk_out [n_heads, n_sets, k] int32: positions within the sequence, ascending, -1 padded.
+ *   n_sets = n_seqs (global) or sum over sequences of ceil(L/block) (block-causal,
+ *   numbered sequence after sequence).
+ * zx_out [T], zv_out [T, n_kv] (nullable, global mode only): the standardized signals.
+ * Tie rule: equal scores are taken lowest position first.
+ */
+size_t dsalt_select_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv,
+                                    int k, int block);
+int dsalt_select_landmarks(int mode, const float* xnorm, const float* vnorm, const int32_t* w,
+                           const float* alpha, const int32_t* cu_seqlens, int n_seqs, int64_t T, int max_seqlen,
+                           int n_heads, int n_kv, int k, int block, int32_t* lmk_out, float* zx_out,
+                           float* zv_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Sparse attention forward over A(i) = W(i) ∪ L(i).
+ * Replaces dsalt_triton_attention / DSALTAttentionFunction.forward
+ *   (dsalt/kernels/dsalt_triton_attn.py:259-311, :337-349) and _dsalt_fwd_kernel (:27-169),
+ *   including _build_landmark_kv (dsalt/kernels/selectors.py:137-159) and
+ *   _build_seq_block_map (selectors.py:37-67), which are done inside.
+ *
+ * q [T, n_heads, head_dim], k/v [T, n_kv, head_dim] (token strides q_stride, kv_stride in
+ *   elements; heads contiguous), dtype DSALT_BF16 / DSALT_F16 (tensor cores) or DSALT_F32
+ *   (fp32 CUDA cores). GQA: head h uses kv head h / (n_heads / n_kv).
+ * w [T] int32 window widths (clamped to >= 1 inside).
+ * lmk [n_heads, n_sets, k_lmk] int32 positions within the sequence (any order, -1 = none);
+ *   lmk_block = 0: one set per sequence; > 0: one set per lmk_block queries.
+ * lmk_bias [n_heads, n_sets, k_lmk] fp32 (nullable): added to landmark logits.
+ * out [T, n_heads, head_dim] in out_dtype; lse [T, n_heads] fp32 (nullable).
+ */
+size_t dsalt_attention_workspace_bytes(int64_t T, int n_seqs, int n_heads, int k_lmk, int lmk_block);
+int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
+                        int head_dim, int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk,
+                        const float* lmk_bias, int k_lmk, int lmk_block, const int32_t* cu_seqlens, int n_seqs,
+                        int max_seqlen, void* out, int out_dtype, float* lse, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/*
+ * The whole inference core of DSALTAttention._packed after the projections and RoPE
+ * (dsalt/modules/dsalt_attention.py:610-625): widths, signals, selection, attention.
+ * Scratch for the intermediates comes from `workspace`
+ * (dsalt_core_workspace_bytes); w_out / lmk_out (nullable) receive copies of the widths
+ * and landmark sets.
+ */
+size_t dsalt_core_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv,
+                                  int head_dim, int k, int block);
+int dsalt_core_forward(int mode, const void* x, int x_dtype, int d_model, int64_t x_stride, const void* gate_w,
+                       const void* gate_b, int gate_dtype, int n_min, int n_max, const float* alpha,
+                       int norm_mode, const void* q, const void* k, const void* v, int qkv_dtype, int n_heads,
+                       int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, int k_lmk, int block,
+                       const int32_t* cu_seqlens, int n_seqs, int64_t T, int max_seqlen, void* out, int out_dtype,
+                       int32_t* w_out, int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSALT_B200_H */
