@@ -34,10 +34,17 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int NST = 4;
-constexpr int NTHREADS = 256;
+constexpr int NTHREADS = 384;  // warpgroup 0: producer (warp 0) + MMA (warp 1); warpgroups 1, 2: softmax A, B
+// Register split with setmaxnreg. The block launches with 168 registers per thread
+// (384 x 168 = 64512); warpgroup 0 gives back to 88 and the two softmax warpgroups take
+// 208: 128 x 88 + 256 x 208 = 64512, and every scheduler (one warp of each warpgroup)
+// holds 88 + 2 x 208 = 504 <= 512 registers per lane. Each setmaxnreg sits at the top of
+// its role's branch so that the compiler allocates each role with its own budget.
+constexpr uint32_t REGS_CTRL = 88, REGS_SOFTMAX = 208;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;
+constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;  // + group * (128 | 64 | HD)
 constexpr int MAX_LMK = 256;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P entries stay below 2^8 between rescales
 
 struct Params {
   const void* k;
@@ -52,7 +59,8 @@ struct Params {
   int n_seqs;
   const int32_t* set_base;
   const int32_t* tile_base;
-  float scale_log2;
+  float scale_log2;  // log2(e) / sqrt(head_dim)
+  float inv_scale;   // sqrt(head_dim): landmark bias in raw-logit units
   uint32_t idesc_qk, idesc_pv;
   void* out;
   int out_dtype;
@@ -107,12 +115,11 @@ struct Smem {
   static constexpr uint32_t Q_OFF = 0;
   static constexpr uint32_t K_OFF = Q_OFF + 2 * TILE_BYTES;
   static constexpr uint32_t V_OFF = K_OFF + NST * TILE_BYTES;
-  static constexpr uint32_t BAR_OFF = V_OFF + NST * TILE_BYTES;
-  static constexpr int NBAR = 2 + 2 + NST + NST + 2 + 2 + 2 + 2 + 2;
+  static constexpr uint32_t MRG_OFF = V_OFF + NST * TILE_BYTES;  // group B -> A: m, l, O[HD] per row
+  static constexpr uint32_t BAR_OFF = MRG_OFF + (HD + 2) * BM * 4;
+  static constexpr int NBAR = 4 + 2 * NST + 10 + 2;
   static constexpr uint32_t MISC_OFF = BAR_OFF + NBAR * 8;
-  static constexpr uint32_t LPOS_OFF = MISC_OFF + 16;
-  static constexpr uint32_t LBIAS_OFF = LPOS_OFF + MAX_LMK * 4;
-  static constexpr uint32_t BYTES = LBIAS_OFF + MAX_LMK * 4;
+  static constexpr uint32_t BYTES = MISC_OFF + 16;
 };
 
 // byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile of HD columns
@@ -123,6 +130,45 @@ __device__ __forceinline__ uint32_t swz_off(int r, int c) {
 }
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmin3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// Masking by exact thresholds. For a row whose valid columns are [a, b],
+//   t1(c) = C·(c − a + ½) ≥ C/2 > 0 exactly when c ≥ a,  t2(c) = C·(b + ½ − c) > 0 exactly when c ≤ b,
+// with C = 2^100 both are exact in fp32 (half-integers below 2^23 scaled by a power of two),
+// so min(x, t1, t2) is x for valid columns and ≤ −2^99 (≈ 0 after exp2) for the others.
+constexpr float MASK_C = 1.2676506002282294e30f;  // 2^100
+constexpr float MASKED_MAX = -1.0e20f;            // a row maximum below this means "no valid column"
+
+// packed fp32 pair ops (sm_100)
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 up2(uint64_t r) {
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(r));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -137,11 +183,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* q_empty = bars + 2;
   uint64_t* kv_full = bars + 4;
   uint64_t* kv_empty = bars + 4 + NST;
-  uint64_t* s_full = bars + 4 + 2 * NST;
+  uint64_t* s_full = bars + 4 + 2 * NST;  // [group]
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_full + 4;
   uint64_t* o_full = s_full + 6;
   uint64_t* o_empty = s_full + 8;
+  uint64_t* mrg_full = s_full + 10;
+  uint64_t* mrg_empty = s_full + 11;
+  float* mrg = reinterpret_cast<float*>(sm + SM::MRG_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + SM::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + SM::MISC_OFF + 4);
 
@@ -158,6 +207,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], 128);
     }
+    mbar_init(mrg_full, 128);
+    mbar_init(mrg_empty, 128);
     for (int i = 0; i < NST; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -173,7 +224,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CTRL));
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
@@ -210,6 +262,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
           }
         } else {
+          // landmark rows gathered into the stage (zero rows for empty slots)
           const int lt = j - f.nwt;
           const int32_t* P = p.lmk + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk;
           for (int rr = lane; rr < BN; rr += 32) {
@@ -236,8 +289,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    const uint32_t tS = tbase + COL_S, tP = tbase + COL_P, tO = tbase + COL_O;
     int g = 0, it = 0;
+    uint32_t n_s[2] = {0, 0}, n_pv[2] = {0, 0}, n_it[2] = {0, 0};
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
       const Item f = item_info(p, item);
@@ -246,59 +299,66 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!mbar_wait(&q_full[qb], (it >> 1) & 1, p.err, 21)) { *abort_flag = 1; break; }
       const uint32_t qaddr = sbase + SM::Q_OFF + qb * SM::TILE_BYTES;
       auto issue_S = [&](int j) -> bool {
-        const int gg = g + j, st = gg % NST, sb = gg & 1;
-        const uint32_t r = (uint32_t)(gg / NST), rs = (uint32_t)(gg >> 1);
+        const int gg = g + j, st = gg % NST, grp = j & 1;
+        const uint32_t r = (uint32_t)(gg / NST);
         if (!mbar_wait(&kv_full[st], r & 1, p.err, 22)) return false;
-        if (!mbar_wait(&s_empty[sb], (rs & 1) ^ 1, p.err, 23)) return false;
+        if (!mbar_wait(&s_empty[grp], (n_s[grp] & 1) ^ 1, p.err, 23)) return false;
         tc_fence_after();
         if (elect_one()) {
           const uint32_t kaddr = sbase + SM::K_OFF + st * SM::TILE_BYTES;
 #pragma unroll
           for (int ks = 0; ks < HD / 16; ++ks) {
             const uint32_t koff = (ks >> 2) * BM * 128 + (ks & 3) * 32;
-            umma_ss(tS + sb * BN, sw128_desc(qaddr + koff, 16, 1024), sw128_desc(kaddr + koff, 16, 1024),
+            umma_ss(tbase + COL_S + grp * BN, sw128_desc(qaddr + koff, 16, 1024), sw128_desc(kaddr + koff, 16, 1024),
                     p.idesc_qk, ks > 0 ? 1u : 0u);
           }
-          umma_commit(&s_full[sb]);
+          umma_commit(&s_full[grp]);
           if (j == NK - 1) umma_commit(&q_empty[qb]);
         }
         __syncwarp();
+        ++n_s[grp];
         return true;
       };
-      if (!issue_S(0)) { *abort_flag = 1; break; }
+      if (!issue_S(0) || (NK > 1 && !issue_S(1))) { *abort_flag = 1; break; }
       for (int j = 0; j < NK; ++j) {
-        if (j + 1 < NK && !issue_S(j + 1)) { *abort_flag = 1; ok = false; break; }
-        const int gg = g + j, st = gg % NST, sb = gg & 1;
-        const uint32_t rs = (uint32_t)(gg >> 1);
-        if (!mbar_wait(&p_full[sb], rs & 1, p.err, 24) || !mbar_wait(&o_empty[sb], (rs & 1) ^ 1, p.err, 25)) {
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
+        const int gg = g + j, st = gg % NST, grp = j & 1;
+        const bool first = j < 2;
+        // the group releases S_j before P_j is ready: refill its buffer first
+        if (j + 2 < NK && !issue_S(j + 2)) { ok = false; break; }
+        if (first && !mbar_wait(&o_empty[grp], (n_it[grp] & 1) ^ 1, p.err, 25)) { ok = false; break; }
+        if (!mbar_wait(&p_full[grp], n_pv[grp] & 1, p.err, 24)) { ok = false; break; }
         tc_fence_after();
         if (elect_one()) {
           const uint32_t vaddr = sbase + SM::V_OFF + st * SM::TILE_BYTES;
 #pragma unroll
           for (int ks = 0; ks < BN / 16; ++ks)
-            umma_ts(tO + sb * HD, tP + sb * 64 + ks * 8, sw128_desc(vaddr + ks * 2048, BM * 128, 1024), p.idesc_pv,
-                    ks > 0 ? 1u : 0u);
-          umma_commit(&o_full[sb]);
+            umma_ts(tbase + COL_O + grp * HD, tbase + COL_P + grp * 64 + ks * 8,
+                    sw128_desc(vaddr + ks * 2048, BM * 128, 1024), p.idesc_pv, (ks > 0 || !first) ? 1u : 0u);
+          umma_commit(&o_full[grp]);
           umma_commit(&kv_empty[st]);
         }
         __syncwarp();
+        ++n_pv[grp];
+        if (first) ++n_it[grp];
       }
+      if (!ok) { *abort_flag = 1; break; }
       g += NK;
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax
-    const int q4 = warp - 4;
-    const int r = q4 * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t tS = tbase + lane_off + COL_S, tP = tbase + lane_off + COL_P, tO = tbase + lane_off + COL_O;
-    const float LOG2E = 1.4426950408889634f;
-    int g = 0;
+  }  // warps 2, 3: no role
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
+    // ------------------------------------------------------------------ softmax groups
+    const int grp = (warp - 4) >> 2;  // 0: warps 4-7, 1: warps 8-11
+    const int quad = warp & 3;        // TMEM lane quadrant of this warp
+    const int r = quad * 32 + lane;   // query row of the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tbase + lane_off + COL_S + grp * BN;
+    const uint32_t tP = tbase + lane_off + COL_P + grp * 64;
+    const uint32_t tO = tbase + lane_off + COL_O + grp * HD;
+    const float sl = p.scale_log2;
+    uint32_t u = 0, n_items_grp = 0, n_done = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n_done) {
       const Item f = item_info(p, item);
       const int NK = f.nwt + f.nlt;
       const int i = f.m0 + r;
@@ -307,103 +367,190 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       wi = wi < 1 ? 1 : wi;
       const int lo_raw = i - wi + 1;
       const int lo = lo_raw < 0 ? 0 : lo_raw;
-      // landmark positions / biases of this item's set, read through L1 (no cross-warp
-      // barrier: every wait in this kernel stays bounded)
+      const int lim = vrow ? max(0, min(f.L, lo_raw)) : 0;  // landmark p valid iff 0 <= p < lim
       const int32_t* Pset = p.lmk + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk;
       const float* Bset = p.lmk_bias ? p.lmk_bias + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk : nullptr;
-      float m_run = -INFINITY, l = 0.0f, m_acc = -INFINITY, m_last = -INFINITY;
-      float acc[HD];
-#pragma unroll
-      for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
-
-      auto consume_O = [&](int gg, float m_t) -> bool {
-        const int sb = gg & 1;
-        const uint32_t rs = (uint32_t)(gg >> 1);
-        if (!mbar_wait(&o_full[sb], rs & 1, p.err, 31)) return false;
-        tc_fence_after();
-        const float fac = (m_acc == -INFINITY) ? 0.0f : ex2_approx(m_acc - m_t);
-#pragma unroll
-        for (int cc = 0; cc < HD / 32; ++cc) {
-          uint32_t o[32];
-          DSALT_TMEM_LD32(tO + sb * HD + cc * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) acc[cc * 32 + e] = fmaf(acc[cc * 32 + e], fac, __uint_as_float(o[e]));
+      // landmark sets are ascending with -1 padding last: as unsigned values they are
+      // non-decreasing, so the valid landmarks of this row (0 <= p < lim) are the first
+      // lcnt entries
+      int lcnt = 0;
+      {
+        int lo_i = 0, hi_i = p.k_lmk;
+        while (lo_i < hi_i) {
+          const int mid = (lo_i + hi_i) >> 1;
+          if ((unsigned)__ldg(Pset + mid) < (unsigned)lim) lo_i = mid + 1;
+          else hi_i = mid;
         }
+        lcnt = lo_i;
+      }
+      float m_acc = -INFINITY, l = 0.0f;  // running max (log2 units, stale by < 2^8) and row sum
+      bool have = false;
+      for (int j = grp; j < NK; j += 2) {
+        if (!mbar_wait(&s_full[grp], u & 1, p.err, 32)) { ok = false; break; }
+        tc_fence_after();
+        // the whole S row in registers: one TMEM round trip, then the buffer is released
+        float x[BN];
+        {
+          uint32_t* xr = reinterpret_cast<uint32_t*>(x);
+          DSALT_TMEM_LD32(tS, xr);
+          DSALT_TMEM_LD32(tS + 32, (xr + 32));
+          DSALT_TMEM_LD32(tS + 64, (xr + 64));
+          DSALT_TMEM_LD32(tS + 96, (xr + 96));
+        }
+        tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&o_empty[sb]);
-        m_acc = m_t;
-        return true;
-      };
-
-      for (int j = 0; j < NK; ++j) {
-        const int gg = g + j, sb = gg & 1;
-        const uint32_t rs = (uint32_t)(gg >> 1);
-        if (!mbar_wait(&s_full[sb], rs & 1, p.err, 32)) { ok = false; break; }
-        tc_fence_after();
+        mbar_arrive(&s_empty[grp]);
+        // valid columns of this row in the tile: [a, b] (window: lo..i; landmarks: the
+        // first lcnt entries of the ascending set, i.e. positions p < lim)
         const bool is_w = j < f.nwt;
-        const int kb = f.kstart + j * BN;
-        const int a = lo - kb, b = i - kb;  // window: valid columns [a, b]
-        const bool full = vrow && is_w && a <= 0 && b >= BN - 1;
         const int lt = j - f.nwt;
-        auto logit = [&](uint32_t bits, int col) -> float {
-          const float s = __uint_as_float(bits) * p.scale_log2;
-          if (full) return s;
-          if (!vrow) return -INFINITY;
-          if (is_w) return (col >= a && col <= b) ? s : -INFINITY;
-          const int c = lt * BN + col;
-          if (c >= p.k_lmk) return -INFINITY;
-          const int pos = __ldg(Pset + c);
-          if (pos < 0 || pos >= f.L || pos > i || pos >= lo_raw) return -INFINITY;
-          return Bset ? s + __ldg(Bset + c) * LOG2E : s;
-        };
-        // pass 1: row max over the valid columns
-        float mt = -INFINITY;
+        const int kb = f.kstart + j * BN;
+        const int a = is_w ? (vrow ? lo - kb : BN) : 0;
+        const int b = is_w ? (vrow ? i - kb : -1) : lcnt - 1 - lt * BN;
+        if (!is_w && Bset != nullptr) {
 #pragma unroll
-        for (int cc = 0; cc < BN / 32; ++cc) {
-          uint32_t sv[32];
-          DSALT_TMEM_LD32(tS + sb * BN + cc * 32, sv);
-          tmem_wait_ld();
+          for (int q = 0; q < 4; ++q) {
+            const int idx = lt * BN + q * 32 + lane;
+            const float bq = idx < p.k_lmk ? __ldg(Bset + idx) * p.inv_scale : 0.0f;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mt = fmaxf(mt, logit(sv[e], cc * 32 + e));
-        }
-        const float m_new = fmaxf(m_run, mt);
-        // pass 2: probabilities, row sum, P -> TMEM (16-bit pairs)
-        float rsum = 0.0f;
-#pragma unroll
-        for (int cc = 0; cc < BN / 32; ++cc) {
-          uint32_t sv[32];
-          DSALT_TMEM_LD32(tS + sb * BN + cc * 32, sv);
-          tmem_wait_ld();
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float x0 = logit(sv[e], cc * 32 + e), x1 = logit(sv[e + 1], cc * 32 + e + 1);
-            const float p0 = (x0 == -INFINITY) ? 0.0f : ex2_approx(x0 - m_new);
-            const float p1 = (x1 == -INFINITY) ? 0.0f : ex2_approx(x1 - m_new);
-            rsum += p0 + p1;
-            pk[e >> 1] = (p.idesc_qk >> 7 & 1) ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+            for (int e = 0; e < 32; ++e) x[q * 32 + e] += __shfl_sync(0xffffffffu, bq, e);
           }
-          DSALT_TMEM_ST16(tP + sb * 64 + cc * 16, pk);
         }
+        // row max: the unmasked maximum bounds the masked one and is used unless it would
+        // move the running max by more than the rescale threshold
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < BN; c += 8) {
+          m0 = fmax3f(m0, x[c], x[c + 1]);
+          m1 = fmax3f(m1, x[c + 2], x[c + 3]);
+          m2 = fmax3f(m2, x[c + 4], x[c + 5]);
+          m3 = fmax3f(m3, x[c + 6], x[c + 7]);
+        }
+        float m_tile = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * sl;
+        const bool row_all = a <= 0 && b >= BN - 1;
+        const float A1 = MASK_C * (0.5f - (float)a), A2 = MASK_C * ((float)b + 0.5f);
+        if (__any_sync(0xffffffffu, !row_all && m_tile > m_acc + RESCALE_THRESHOLD)) {
+          m0 = m1 = m2 = m3 = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < BN; c += 4) {
+            m0 = fmaxf(m0, fmin3f(x[c], fmaf(MASK_C, (float)c, A1), fmaf(-MASK_C, (float)c, A2)));
+            m1 = fmaxf(m1, fmin3f(x[c + 1], fmaf(MASK_C, (float)(c + 1), A1), fmaf(-MASK_C, (float)(c + 1), A2)));
+            m2 = fmaxf(m2, fmin3f(x[c + 2], fmaf(MASK_C, (float)(c + 2), A1), fmaf(-MASK_C, (float)(c + 2), A2)));
+            m3 = fmaxf(m3, fmin3f(x[c + 3], fmaf(MASK_C, (float)(c + 3), A1), fmaf(-MASK_C, (float)(c + 3), A2)));
+          }
+          m_tile = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * sl;
+          if (m_tile < MASKED_MAX) m_tile = -INFINITY;
+        }
+        // rescale only when the row max grows by more than the threshold
+        const bool need = m_tile > m_acc + RESCALE_THRESHOLD;
+        const float m_new = need ? m_tile : m_acc;
+        if (have) {
+          // previous P·V of this group done: P buffer free, O may be rescaled
+          if (!mbar_wait(&o_full[grp], (u - 1) & 1, p.err, 33)) { ok = false; break; }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, need)) {
+            const float fac = need ? ex2_approx(m_acc - m_new) : 1.0f;
+#pragma unroll 1
+            for (int cc = 0; cc < HD / 16; ++cc) {
+              uint32_t o[16];
+              DSALT_TMEM_LD16(tO + cc * 16, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
+              DSALT_TMEM_ST16(tO + cc * 16, o);
+            }
+            tmem_wait_st();
+            l *= fac;
+          }
+        } else if (need) {
+          l = 0.0f;  // first tile of the group in this item: O is written, not accumulated
+        }
+        m_acc = m_new;
+        const float mu = (m_acc == -INFINITY) ? 0.0f : m_acc;
+        const uint64_t sl2 = pk2(sl, sl), nmu2 = pk2(-mu, -mu);
+        uint64_t s0 = pk2(0.f, 0.f), s1 = s0;
+        const bool bf = (p.idesc_qk >> 7) & 1;
+        // probabilities, row sum, P -> TMEM as 16-bit pairs. Per 32-column chunk the warp
+        // masks only when some lane keeps part of it, and skips the exponentials when no
+        // lane keeps any of it.
+#pragma unroll
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          const int c0 = cc * 32;
+          const bool keep_none = b < c0 || a > c0 + 31;
+          const bool keep_all = a <= c0 && b >= c0 + 31;
+          uint32_t pk[16];
+          if (__all_sync(0xffffffffu, keep_none)) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) pk[e] = 0u;
+          } else {
+            float* xc = x + c0;
+            if (!__all_sync(0xffffffffu, keep_all)) {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                xc[e] = fmin3f(xc[e], fmaf(MASK_C, (float)(c0 + e), A1), fmaf(-MASK_C, (float)(c0 + e), A2));
+            }
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const float2 y0 = up2(fma2(pk2(xc[e], xc[e + 1]), sl2, nmu2));
+              const float2 y1 = up2(fma2(pk2(xc[e + 2], xc[e + 3]), sl2, nmu2));
+              const float p0 = ex2_approx(y0.x), p1 = ex2_approx(y0.y);
+              const float p2 = ex2_approx(y1.x), p3 = ex2_approx(y1.y);
+              s0 = add2(s0, pk2(p0, p1));
+              s1 = add2(s1, pk2(p2, p3));
+              pk[e >> 1] = bf ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+              pk[(e >> 1) + 1] = bf ? pack_bf16x2(p2, p3) : pack_f16x2(p2, p3);
+            }
+          }
+          DSALT_TMEM_ST16(tP + cc * 16, pk);
+        }
+        const float2 ss = up2(add2(s0, s1));
+        l += ss.x + ss.y;
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&s_empty[sb]);
-        mbar_arrive(&p_full[sb]);
-        const float corr = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_new);
-        l = fmaf(l, corr, rsum);
-        const float m_prev_tile = m_last;
-        m_last = m_new;
-        m_run = m_new;
-        if (j >= 1 && !consume_O(gg - 1, m_prev_tile)) { ok = false; break; }
+        mbar_arrive(&p_full[grp]);
+        have = true;
+        ++u;
       }
-      if (!ok) { *abort_flag = 1; break; }
-      if (!consume_O(g + NK - 1, m_last)) { *abort_flag = 1; break; }
-      g += NK;
-      // epilogue
+      if (!ok) break;
+      // this group's O of the item, loaded once its last P·V is done
+      float acc[HD];
+      if (have) {
+        if (!mbar_wait(&o_full[grp], (u - 1) & 1, p.err, 34)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < HD / 32; ++cc) {
+          uint32_t* orr = reinterpret_cast<uint32_t*>(acc + cc * 32);
+          DSALT_TMEM_LD32(tO + cc * 32, orr);
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&o_empty[grp]);
+        ++n_items_grp;
+      } else {
+#pragma unroll
+        for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
+      }
+      if (grp == 1) {
+        if (!mbar_wait(mrg_empty, (n_done & 1) ^ 1, p.err, 35)) { ok = false; break; }
+        mrg[r] = m_acc;
+        mrg[BM + r] = l;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) mrg[(2 + d) * BM + r] = acc[d];
+        mbar_arrive(mrg_full);
+        continue;
+      }
+      if (!mbar_wait(mrg_full, n_done & 1, p.err, 36)) { ok = false; break; }
+      const float mB = mrg[r], lB = mrg[BM + r];
+      const float m = fmaxf(m_acc, mB);
+      const float fA = (m_acc == -INFINITY) ? 0.0f : ex2_approx(m_acc - m);
+      const float fB = (mB == -INFINITY) ? 0.0f : ex2_approx(mB - m);
+#pragma unroll
+      for (int d = 0; d < HD; ++d) acc[d] = acc[d] * fA + mrg[(2 + d) * BM + r] * fB;
+      const float lt = l * fA + lB * fB;
+      mbar_arrive(mrg_empty);
       if (vrow) {
-        const bool good = l > 1e-9f;
-        const float inv = good ? 1.0f / l : 0.0f;
+        const bool good = lt > 1e-9f;
+        const float inv = good ? 1.0f / lt : 0.0f;
         const int64_t row = (int64_t)(f.start + i);
         if (p.out_dtype == DSALT_F32) {
           float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (row * p.H + f.h) * HD);
@@ -415,17 +562,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const bool bf = p.out_dtype == DSALT_BF16;
 #pragma unroll
           for (int d = 0; d < HD; d += 8) {
-            uint4 u;
-            u.x = bf ? pack_bf16x2(acc[d] * inv, acc[d + 1] * inv) : pack_f16x2(acc[d] * inv, acc[d + 1] * inv);
-            u.y = bf ? pack_bf16x2(acc[d + 2] * inv, acc[d + 3] * inv) : pack_f16x2(acc[d + 2] * inv, acc[d + 3] * inv);
-            u.z = bf ? pack_bf16x2(acc[d + 4] * inv, acc[d + 5] * inv) : pack_f16x2(acc[d + 4] * inv, acc[d + 5] * inv);
-            u.w = bf ? pack_bf16x2(acc[d + 6] * inv, acc[d + 7] * inv) : pack_f16x2(acc[d + 6] * inv, acc[d + 7] * inv);
-            o[d / 8] = u;
+            uint4 q4;
+            q4.x = bf ? pack_bf16x2(acc[d] * inv, acc[d + 1] * inv) : pack_f16x2(acc[d] * inv, acc[d + 1] * inv);
+            q4.y = bf ? pack_bf16x2(acc[d + 2] * inv, acc[d + 3] * inv) : pack_f16x2(acc[d + 2] * inv, acc[d + 3] * inv);
+            q4.z = bf ? pack_bf16x2(acc[d + 4] * inv, acc[d + 5] * inv) : pack_f16x2(acc[d + 4] * inv, acc[d + 5] * inv);
+            q4.w = bf ? pack_bf16x2(acc[d + 6] * inv, acc[d + 7] * inv) : pack_f16x2(acc[d + 6] * inv, acc[d + 7] * inv);
+            o[d / 8] = q4;
           }
         }
-        if (p.lse) p.lse[row * p.H + f.h] = good ? (m_last + log2f(l)) * 0.6931471805599453f : -INFINITY;
+        if (p.lse) p.lse[row * p.H + f.h] = good ? (m + log2f(lt)) * 0.6931471805599453f : -INFINITY;
       }
     }
+    if (!ok) *abort_flag = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -502,6 +650,7 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   p.set_base = set_base;
   p.tile_base = tile_base;
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
+  p.inv_scale = (float)sqrt((double)HD);
   const uint32_t ab = dtype == DSALT_BF16 ? 1u : 0u;
   p.idesc_qk = umma_idesc_f16(ab, 0, 0, BM, BN);
   p.idesc_pv = umma_idesc_f16(ab, 0, 1, BM, HD);

@@ -165,6 +165,19 @@ def _norms_only(x, v, head_dim, norm_round):
 
 
 # --------------------------------------------------------------------------- attention
+def normalize_landmarks(lmk_indices, lmk_bias=None):
+    """Each landmark set in the kernel's format: valid positions ascending, ``-1`` last
+    (the reference leaves the order unspecified). The bias follows its landmark."""
+    lmk = lmk_indices.to(torch.int32)
+    key = torch.where(lmk < 0, torch.full_like(lmk, torch.iinfo(torch.int32).max), lmk)
+    key, order = torch.sort(key, dim=-1, stable=True)
+    lmk = torch.where(key == torch.iinfo(torch.int32).max, torch.full_like(key, -1), key).contiguous()
+    bias = None
+    if lmk_bias is not None:
+        bias = torch.gather(lmk_bias.to(torch.float32), -1, order).contiguous()
+    return lmk, bias
+
+
 def dsalt_attention(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, *, lmk_block: int = 0, out_dtype=None,
                     cu_list=None, return_lse: bool = False):
     """Drop-in for ``dsalt_triton_attention(q, k, v, lmk_indices, lmk_bias, w_sizes,
@@ -193,9 +206,8 @@ def dsalt_attention(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, *, lmk_
     cu_h = _host_cu(cu_seqlens, cu_list)
     S = len(cu_h) - 1
     maxL = max([cu_h[i + 1] - cu_h[i] for i in range(S)] + [0])
-    lmk = lmk_indices.to(torch.int32).contiguous()
+    lmk, bias = normalize_landmarks(lmk_indices, lmk_bias)
     kl = int(lmk.shape[-1])
-    bias = None if lmk_bias is None else lmk_bias.to(torch.float32).contiguous()
     odt = out_dtype if out_dtype is not None else (dt if dt != torch.float32 else torch.float32)
     out = torch.empty(T, H, D, dtype=odt, device=q.device)
     lse = torch.empty(T, H, dtype=torch.float32, device=q.device) if return_lse else None

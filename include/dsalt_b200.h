@@ -102,7 +102,9 @@ int dsalt_select_landmarks(int mode, const float* xnorm, const float* vnorm, con
  *   elements; heads contiguous), dtype DSALT_BF16 / DSALT_F16 (tensor cores) or DSALT_F32
  *   (fp32 CUDA cores). GQA: head h uses kv head h / (n_heads / n_kv).
  * w [T] int32 window widths (clamped to >= 1 inside).
- * lmk [n_heads, n_sets, k_lmk] int32 positions within the sequence (any order, -1 = none);
+ * lmk [n_heads, n_sets, k_lmk] int32 positions within the sequence, -1 = none. For the
+ *   bf16/fp16 path every set must list its positions ascending with the -1 entries last
+ *   (the format dsalt_select_landmarks writes); the fp32 path accepts any order.
  *   lmk_block = 0: one set per sequence; > 0: one set per lmk_block queries.
  * lmk_bias [n_heads, n_sets, k_lmk] fp32 (nullable): added to landmark logits.
  * out [T, n_heads, head_dim] in out_dtype; lse [T, n_heads] fp32 (nullable).

@@ -247,10 +247,32 @@ def test_module_matches_reference_fixture(name):
     with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["dtype"] == "bf16"):
         out, aux = mod(x, cu_t, cu_list=cu)
     got = out.float().cpu().numpy()[d["rows"]]
-    err = np.abs(got - d["mod_rows"]).max()
-    # module outputs pass through library GEMMs, and the reference's attention rounds its
-    # fp32 inputs to fp16 (dsalt_triton_attn.py:266): the bf16 tolerance applies
-    assert err <= BF16_TOL, err
+    # (1) against the oracle's module output: exact attention, rounded to the compute
+    #     dtype, then the same out_proj GEMM
+    rows = d["rows"]
+    q, k, v, _ = C.project(cfg, params, C.make_x(cfg))
+    lb = 0 if cfg["mode"] == "global" else cfg["block"]
+    att, _ = O.attention_forward(q.float().numpy(), k.float().numpy(), v.float().numpy(), d["w"], d["lmk"], cu,
+                                 lmk_block=lb, rows=rows)
+    dt = C.torch_dtype(cfg)
+    a = torch.tensor(att[rows], dtype=torch.float32).to(dt).reshape(len(rows), -1).to(_dev())
+    W = params["out_proj.weight"].to(dt).to(_dev())
+    exp = torch.nn.functional.linear(a, W).float().cpu().numpy().astype(np.float64)
+    if cfg["dtype"] == "fp32":
+        assert np.abs(got - exp).max() <= FP32_TOL
+    else:
+        # both sides round twice in bf16 (attention output, out_proj output)
+        excess = (np.abs(got - exp) - 2 * 2.0 ** -7 * np.abs(exp)).max()
+        assert excess <= BF16_TOL, excess
+    # (2) against the reference's own module rows. The reference rounds twice in the
+    #     compute dtype (attention output, then out_proj), its block-causal forward runs
+    #     q·k and P·V as autocast bf16 matmuls, and its Triton path casts fp32 inputs to
+    #     fp16 (dsalt_triton_attn.py:266). Its rows differ from an exact attention
+    #     followed by the same out_proj by up to ~4e-3 (measured on these fixtures), so
+    #     the check against them is 5e-3 beyond two ulps of the value.
+    ref = d["mod_rows"].astype(np.float64)
+    excess = (np.abs(got - ref) - 2 * 2.0 ** -7 * np.abs(ref)).max()
+    assert excess <= 5e-3, excess
 
 
 # --------------------------------------------------------------------------- full size
