@@ -3,23 +3,26 @@
 // Semantics of the reference's inference kernel (dsalt/kernels/dsalt_triton_attn.py:27-169):
 // query i of a sequence attends to its window j ∈ [max(0, i−w(i)+1), i] and to the
 // landmarks p of its set with 0 ≤ p < L, p ≤ i and p < i−w(i)+1 (the de-duplicating
-// rule of :132-135); logits q·k·D^-½ (+ optional landmark bias); online softmax with
-// fp32 statistics, P rounded to the input dtype for the P·V product (as the reference's
+// rule of :132-135); logits q·k·D^-½ (+ optional landmark bias); softmax statistics in
+// fp32, P rounded to the input dtype for the P·V product (as the reference's
 // tl.dot(p.to(bf16), v)); rows with softmax mass ≤ 1e-9 are zero.
 //
 // Work item = (128-query tile, head); persistent CTAs, one per SM. Per item the key
-// axis is a band of 128-key window tiles starting at max(0, m0 − max_w + 1) plus
-// ceil(k/128) landmark tiles. Roles (256 threads):
-//   warp 0  producer: TMA (no multicast) for the Q tile and the K/V window tiles into a
-//           4-stage ring; landmark K/V rows gathered with cp.async into the same ring
-//           (replaces _build_landmark_kv, dsalt/kernels/selectors.py:137-159);
-//   warp 1  TMEM allocation and the single-thread MMA issuer:
-//           S = Q·Kᵀ (SS form, M=128 N=128 K=16 steps) into TMEM S[2],
-//           O_j = P_j·V_j (TS form: P read from TMEM, V from smem, N = head_dim) into O[2];
-//   warps 4-7 softmax: row r ↔ TMEM lane r; masks, running max/sum in registers, P
-//           written back to TMEM as packed 16-bit pairs, O_j accumulated in registers
-//           with the max-rescale, epilogue to global memory.
-// TMEM columns: S0 S1 (128 each) | P0 P1 (64 each) | O0 O1 (head_dim each) — 512 total.
+// axis is a band of 128-key window tiles ending at the tile's last row and reaching back
+// to max(0, m0 − max_w + 1), plus ceil(k/128) landmark tiles; the diagonal tile goes
+// first, then the landmark tiles, then the other window tiles. Each CTA runs two
+// independent pipelines (A, B) on alternate items; a pipeline is
+//   a producer warp   TMA (no multicast) of the Q tile and the K/V window tiles into a
+//                     3-stage K ring and a 2-stage V ring; landmark K/V rows gathered by
+//                     one-row TMA boxes into the same rings (replaces _build_landmark_kv,
+//                     selectors.py:137-159);
+//   an MMA warp       one thread issues S = Q·Kᵀ (SS form) into TMEM and O += P·V (TS
+//                     form: P read from TMEM, V from smem) into a TMEM accumulator;
+//   4 softmax warps   row r ↔ TMEM lane r: the S row is read once into registers,
+//                     masked, exponentiated; P goes back to TMEM as 16-bit pairs; O is
+//                     rescaled in TMEM only when the running max grows by more than 2^8.
+// TMEM (512 columns): per pipeline S (128) | P (64) | O (head_dim).
+// Warps: 0/1 producer/MMA of A, 2/3 producer/MMA of B, 4-7 softmax A, 8-11 softmax B.
 // Every mbarrier wait is bounded (common.cuh) and reports to the device status word.
 #include <cuda.h>
 
@@ -33,16 +36,22 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int NST = 4;
-constexpr int NTHREADS = 384;  // warpgroup 0: producer (warp 0) + MMA (warp 1); warpgroups 1, 2: softmax A, B
+constexpr int NPIPE = 2;
+constexpr int NSK = 3;          // K stages per pipeline (released when S = Q·Kᵀ completes)
+constexpr int NSV = 2;          // V stages per pipeline (released when O += P·V completes)
+constexpr int NQB = 1;          // Q buffers per pipeline
+constexpr int NIS = 2;          // item-description slots per pipeline
+constexpr int NTHREADS = 384;
 // Register split with setmaxnreg. The block launches with 168 registers per thread
-// (384 x 168 = 64512); warpgroup 0 gives back to 88 and the two softmax warpgroups take
-// 208: 128 x 88 + 256 x 208 = 64512, and every scheduler (one warp of each warpgroup)
-// holds 88 + 2 x 208 = 504 <= 512 registers per lane. Each setmaxnreg sits at the top of
-// its role's branch so that the compiler allocates each role with its own budget.
+// (384 x 168 = 64512); warpgroup 0 (producers, MMA issuers) gives back to 88 and the two
+// softmax warpgroups take 208: 128 x 88 + 256 x 208 = 64512, and every scheduler (one
+// warp of each warpgroup) holds 88 + 2 x 208 = 504 <= 512 registers per lane. Each
+// setmaxnreg sits at the top of its role's branch so that the compiler allocates each
+// role with its own budget.
 constexpr uint32_t REGS_CTRL = 88, REGS_SOFTMAX = 208;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;  // + group * (128 | 64 | HD)
+constexpr uint32_t PIPE_COLS = 256;                 // S 128 | P 64 | O 64
+constexpr uint32_t COL_S = 0, COL_P = 128, COL_O = 192;
 constexpr int MAX_LMK = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P entries stay below 2^8 between rescales
 
@@ -99,26 +108,43 @@ __device__ __forceinline__ Item item_info(const Params& p, int item) {
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+  // window tiles end at the tile's last row, so that the last one holds every row's
+  // diagonal key; the first may start before the sequence (those keys are masked)
   const int hi = min(f.m0 + BM - 1, f.L - 1);
-  f.kstart = max(0, f.m0 - wm + 1);
-  f.nwt = (hi - f.kstart + BN) / BN;
+  const int kmin = max(0, f.m0 - wm + 1);
+  f.nwt = (hi - kmin + BN) / BN;
+  f.kstart = hi + 1 - f.nwt * BN;
   f.nlt = (p.k_lmk + BN - 1) / BN;
   f.n_sets = p.lmk_block ? p.set_base[p.n_seqs] : p.n_seqs;
   f.set = p.lmk_block ? p.set_base[f.s] + f.m0 / p.lmk_block : f.s;
   return f;
 }
 
+// Processing order of an item's key tiles: the diagonal window tile first (every valid
+// row gets a finite running max at once), then the landmark tiles, then the remaining
+// window tiles right to left. Returns the window-tile index, or -1 - (landmark tile).
+__device__ __forceinline__ int tile_at(const Item& f, int t) {
+  if (t == 0) return f.nwt - 1;
+  if (t <= f.nlt) return -t;
+  return f.nwt - 1 - (t - f.nlt);
+}
+
 template <int HD>
 struct Smem {
   static constexpr int NA = HD / 64;                       // 128-byte swizzle atoms per row
   static constexpr uint32_t TILE_BYTES = BM * HD * 2;      // one 128 x HD 16-bit tile
-  static constexpr uint32_t Q_OFF = 0;
-  static constexpr uint32_t K_OFF = Q_OFF + 2 * TILE_BYTES;
-  static constexpr uint32_t V_OFF = K_OFF + NST * TILE_BYTES;
-  static constexpr uint32_t MRG_OFF = V_OFF + NST * TILE_BYTES;  // group B -> A: m, l, O[HD] per row
-  static constexpr uint32_t BAR_OFF = MRG_OFF + (HD + 2) * BM * 4;
-  static constexpr int NBAR = 4 + 2 * NST + 10 + 2;
-  static constexpr uint32_t MISC_OFF = BAR_OFF + NBAR * 8;
+  static constexpr uint32_t PIPE_BYTES = (NQB + NSK + NSV) * TILE_BYTES;
+  static constexpr uint32_t Q_OFF = 0;                     // + pipe * PIPE_BYTES
+  static constexpr uint32_t K_OFF = NQB * TILE_BYTES;
+  static constexpr uint32_t V_OFF = K_OFF + NSK * TILE_BYTES;
+  // item slots: description, per-row window start and landmark count, landmark positions
+  static constexpr uint32_t SLOT_BYTES = 64 + 2 * BM * 4 + MAX_LMK * 4;
+  static constexpr uint32_t SLOT_OFF = NPIPE * PIPE_BYTES;  // + (pipe * NIS + slot) * SLOT_BYTES
+  static constexpr uint32_t BAR_OFF = SLOT_OFF + NPIPE * NIS * SLOT_BYTES;
+  // per pipeline: q_full[NQB] q_empty[NQB] k_full[NSK] k_empty[NSK] v_full[NSV] v_empty[NSV]
+  // s_full s_empty p_full o_full o_empty item_full[NIS] item_empty[NIS]
+  static constexpr int NBAR_PIPE = 2 * NQB + 2 * NSK + 2 * NSV + 5 + 2 * NIS;
+  static constexpr uint32_t MISC_OFF = BAR_OFF + NPIPE * NBAR_PIPE * 8;
   static constexpr uint32_t BYTES = MISC_OFF + 16;
 };
 
@@ -128,8 +154,6 @@ __device__ __forceinline__ uint32_t swz_off(int r, int c) {
   const int atom = c >> 3, cc = c & 7;
   return (uint32_t)(atom * BM * 128 + r * 128 + ((cc ^ (r & 7)) << 4));
 }
-
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float d;
@@ -142,7 +166,7 @@ __device__ __forceinline__ float fmin3f(float a, float b, float c) {
   return d;
 }
 // Masking by exact thresholds. For a row whose valid columns are [a, b],
-//   t1(c) = C·(c − a + ½) ≥ C/2 > 0 exactly when c ≥ a,  t2(c) = C·(b + ½ − c) > 0 exactly when c ≤ b,
+//   t1(c) = C·(c − a + ½) > 0 exactly when c ≥ a,  t2(c) = C·(b + ½ − c) > 0 exactly when c ≤ b,
 // with C = 2^100 both are exact in fp32 (half-integers below 2^23 scaled by a power of two),
 // so min(x, t1, t2) is x for valid columns and ≤ −2^99 (≈ 0 after exp2) for the others.
 constexpr float MASK_C = 1.2676506002282294e30f;  // 2^100
@@ -170,50 +194,54 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return d;
 }
 
+struct PipeBars {
+  uint64_t *q_full, *q_empty, *k_full, *k_empty, *v_full, *v_empty, *s_full, *s_empty, *p_full, *o_full, *o_empty,
+      *it_full, *it_empty;
+};
+
+// one item's description as the producer publishes it to the MMA and softmax warps
+struct Slot {
+  Item f;
+  int pad[16 - sizeof(Item) / 4];
+  int32_t lo[BM];    // per row: first window key (>= 0), or BM-clamped sentinel for rows past L
+  int32_t lcnt[BM];  // per row: number of landmarks of the set that the row may use
+  int32_t pos[MAX_LMK];
+};
+static_assert(sizeof(Item) <= 64, "item description must fit the slot header");
+
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kr,
+                       const __grid_constant__ CUtensorMap tm_vr, const Params p) {
   using SM = Smem<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t sbase = smem_u32(sm);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + SM::BAR_OFF);
-  uint64_t* q_full = bars;
-  uint64_t* q_empty = bars + 2;
-  uint64_t* kv_full = bars + 4;
-  uint64_t* kv_empty = bars + 4 + NST;
-  uint64_t* s_full = bars + 4 + 2 * NST;  // [group]
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_full + 4;
-  uint64_t* o_full = s_full + 6;
-  uint64_t* o_empty = s_full + 8;
-  uint64_t* mrg_full = s_full + 10;
-  uint64_t* mrg_empty = s_full + 11;
-  float* mrg = reinterpret_cast<float*>(sm + SM::MRG_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + SM::MISC_OFF);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + SM::MISC_OFF + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_items = p.tile_base[p.n_seqs] * p.H;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+    for (int pp = 0; pp < NPIPE; ++pp) {
+      uint64_t* b = reinterpret_cast<uint64_t*>(sm + SM::BAR_OFF) + pp * SM::NBAR_PIPE;
+      for (int i = 0; i < NQB; ++i) {
+        mbar_init(b + i, 1);        // q_full
+        mbar_init(b + NQB + i, 1);  // q_empty
+      }
+      for (int i = 0; i < 2 * NSK + 2 * NSV; ++i) mbar_init(b + 2 * NQB + i, 1);  // K/V full and empty
+      uint64_t* t = b + 2 * NQB + 2 * NSK + 2 * NSV;
+      mbar_init(t + 0, 1);    // s_full
+      mbar_init(t + 1, 128);  // s_empty
+      mbar_init(t + 2, 128);  // p_full
+      mbar_init(t + 3, 1);    // o_full
+      mbar_init(t + 4, 128);  // o_empty
+      for (int i = 0; i < NIS; ++i) {
+        mbar_init(t + 5 + i, 1);              // item_full: the producer publishes
+        mbar_init(t + 5 + NIS + i, 128 + 1);  // item_empty: 128 softmax threads + the MMA issuer
+      }
     }
-    mbar_init(mrg_full, 128);
-    mbar_init(mrg_empty, 128);
-    for (int i = 0; i < NST; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
-    *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -224,169 +252,210 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+
+  // pipeline of this warp and its barriers / buffers
+  const int pipe = warp < 4 ? (warp >> 1) : ((warp - 4) >> 2);
+  PipeBars B;
+  {
+    uint64_t* b = reinterpret_cast<uint64_t*>(sm + SM::BAR_OFF) + pipe * SM::NBAR_PIPE;
+    B.q_full = b;
+    B.q_empty = b + NQB;
+    B.k_full = b + 2 * NQB;
+    B.k_empty = B.k_full + NSK;
+    B.v_full = B.k_empty + NSK;
+    B.v_empty = B.v_full + NSV;
+    uint64_t* t = b + 2 * NQB + 2 * NSK + 2 * NSV;
+    B.s_full = t;
+    B.s_empty = t + 1;
+    B.p_full = t + 2;
+    B.o_full = t + 3;
+    B.o_empty = t + 4;
+    B.it_full = t + 5;
+    B.it_empty = t + 5 + NIS;
+  }
+  Slot* slots = reinterpret_cast<Slot*>(sm + SM::SLOT_OFF) + pipe * NIS;
+  const uint32_t pbase = sbase + pipe * SM::PIPE_BYTES;
+  const uint32_t tpipe = tbase + pipe * PIPE_COLS;
+  // items of this pipeline: the CTA's items alternate between the two pipelines
+  const int item0 = blockIdx.x + pipe * gridDim.x, istride = NPIPE * gridDim.x;
+
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CTRL));
-  if (warp == 0) {
-    // ------------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-    }
-    int g = 0, it = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
-      const Item f = item_info(p, item);
-      const int qb = it & 1;
-      if (!mbar_wait(&q_empty[qb], ((it >> 1) & 1) ^ 1, p.err, 11)) { *abort_flag = 1; break; }
+    if ((warp & 1) == 0) {
+      // ---------------------------------------------------------------- producer
       if (lane == 0) {
-        mbar_arrive_expect_tx(&q_full[qb], SM::TILE_BYTES);
-        for (int a = 0; a < SM::NA; ++a)
-          tma_load_3d(sbase + SM::Q_OFF + qb * SM::TILE_BYTES + a * BM * 128, &tm_q, &q_full[qb], a * 64, f.h,
-                      f.start + f.m0);
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
       }
-      const int NK = f.nwt + f.nlt;
+      int g = 0, it = 0;
       bool ok = true;
-      for (int j = 0; j < NK; ++j, ++g) {
-        const int st = g % NST;
-        const uint32_t r = (uint32_t)(g / NST);
-        if (!mbar_wait(&kv_empty[st], (r & 1) ^ 1, p.err, 12) || *abort_flag) { *abort_flag = 1; ok = false; break; }
-        const uint32_t kdst = sbase + SM::K_OFF + st * SM::TILE_BYTES;
-        const uint32_t vdst = sbase + SM::V_OFF + st * SM::TILE_BYTES;
-        if (j < f.nwt) {
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&kv_full[st], 2 * SM::TILE_BYTES);
-            const int row = f.start + f.kstart + j * BN;
-            for (int a = 0; a < SM::NA; ++a) {
-              tma_load_3d(kdst + a * BM * 128, &tm_k, &kv_full[st], a * 64, f.hk, row);
-              tma_load_3d(vdst + a * BM * 128, &tm_v, &kv_full[st], a * 64, f.hk, row);
-            }
+      for (int item = item0; item < n_items && ok; item += istride, ++it) {
+        const Item f = item_info(p, item);
+        // publish the item: description, per-row window starts and landmark counts
+        const int sl_i = it % NIS;
+        if (!mbar_wait(&B.it_empty[sl_i], ((it / NIS) & 1) ^ 1, p.err, 13)) break;
+        Slot& S = slots[sl_i];
+        if (lane == 0) S.f = f;
+        const int32_t* P = p.lmk + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk;
+        for (int c = lane; c < f.nlt * BN; c += 32) S.pos[c] = c < p.k_lmk ? __ldg(P + c) : -1;
+        __syncwarp();
+        for (int rr = lane; rr < BM; rr += 32) {
+          const int i = f.m0 + rr;
+          const bool vrow = i < f.L;
+          int wi = vrow ? __ldg(p.w + f.start + i) : 1;
+          wi = wi < 1 ? 1 : wi;
+          const int lo_raw = i - wi + 1;
+          S.lo[rr] = vrow ? (lo_raw < 0 ? 0 : lo_raw) : 0x3fffffff;
+          // sets are ascending with -1 last: as unsigned values non-decreasing, so the
+          // landmarks the row may use (0 <= p < min(L, i-w+1)) are a prefix of the set
+          const int lim = vrow ? max(0, min(f.L, lo_raw)) : 0;
+          int a0 = 0, a1 = p.k_lmk;
+          while (a0 < a1) {
+            const int mid = (a0 + a1) >> 1;
+            if ((unsigned)S.pos[mid] < (unsigned)lim) a0 = mid + 1;
+            else a1 = mid;
           }
-        } else {
-          // landmark rows gathered into the stage (zero rows for empty slots)
-          const int lt = j - f.nwt;
-          const int32_t* P = p.lmk + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk;
-          for (int rr = lane; rr < BN; rr += 32) {
-            const int idx = lt * BN + rr;
-            const int pos = idx < p.k_lmk ? P[idx] : -1;
-            const bool valid = pos >= 0 && pos < f.L;
-            const int64_t off = valid ? ((int64_t)(f.start + pos) * p.kv_stride + (int64_t)f.hk * HD) * 2 : 0;
-            const char* ks = reinterpret_cast<const char*>(p.k) + off;
-            const char* vs = reinterpret_cast<const char*>(p.v) + off;
-#pragma unroll
-            for (int c = 0; c < HD / 8; ++c) {
-              const uint32_t o = swz_off<HD>(rr, c);
-              cp_async_16(kdst + o, ks + c * 16, valid ? 16u : 0u);
-              cp_async_16(vdst + o, vs + c * 16, valid ? 16u : 0u);
-            }
-          }
-          cp_async_wait_all();
-          fence_proxy_async_smem();
+          S.lcnt[rr] = a0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.it_full[sl_i]);
+        const int qb = it % NQB;
+        if (!mbar_wait(&B.q_empty[qb], ((it / NQB) & 1) ^ 1, p.err, 11)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&B.q_full[qb], SM::TILE_BYTES);
+          for (int a = 0; a < SM::NA; ++a)
+            tma_load_3d(pbase + SM::Q_OFF + qb * SM::TILE_BYTES + a * BM * 128, &tm_q, &B.q_full[qb], a * 64, f.h,
+                        f.start + f.m0);
+        }
+        const int NK = f.nwt + f.nlt;
+        for (int t = 0; t < NK; ++t, ++g) {
+          const int jt = tile_at(f, t);
+          const int sk = g % NSK, sv = g % NSV;
+          const uint32_t kdst = pbase + SM::K_OFF + sk * SM::TILE_BYTES;
+          const uint32_t vdst = pbase + SM::V_OFF + sv * SM::TILE_BYTES;
+          if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
+          if (lane == 0) mbar_arrive_expect_tx(&B.k_full[sk], SM::TILE_BYTES);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&kv_full[st]);
-        }
-      }
-      if (!ok) break;
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    int g = 0, it = 0;
-    uint32_t n_s[2] = {0, 0}, n_pv[2] = {0, 0}, n_it[2] = {0, 0};
-    bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-      const Item f = item_info(p, item);
-      const int NK = f.nwt + f.nlt;
-      const int qb = it & 1;
-      if (!mbar_wait(&q_full[qb], (it >> 1) & 1, p.err, 21)) { *abort_flag = 1; break; }
-      const uint32_t qaddr = sbase + SM::Q_OFF + qb * SM::TILE_BYTES;
-      auto issue_S = [&](int j) -> bool {
-        const int gg = g + j, st = gg % NST, grp = j & 1;
-        const uint32_t r = (uint32_t)(gg / NST);
-        if (!mbar_wait(&kv_full[st], r & 1, p.err, 22)) return false;
-        if (!mbar_wait(&s_empty[grp], (n_s[grp] & 1) ^ 1, p.err, 23)) return false;
-        tc_fence_after();
-        if (elect_one()) {
-          const uint32_t kaddr = sbase + SM::K_OFF + st * SM::TILE_BYTES;
-#pragma unroll
-          for (int ks = 0; ks < HD / 16; ++ks) {
-            const uint32_t koff = (ks >> 2) * BM * 128 + (ks & 3) * 32;
-            umma_ss(tbase + COL_S + grp * BN, sw128_desc(qaddr + koff, 16, 1024), sw128_desc(kaddr + koff, 16, 1024),
-                    p.idesc_qk, ks > 0 ? 1u : 0u);
+          if (jt >= 0) {
+            if (lane == 0)
+              for (int a = 0; a < SM::NA; ++a)
+                tma_load_3d(kdst + a * BM * 128, &tm_k, &B.k_full[sk], a * 64, f.hk, f.start + f.kstart + jt * BN);
+          } else {
+            // landmark rows, one-row TMA boxes; unused slots read row start-1 (or past the
+            // end, zero-filled): those columns are masked by the row's landmark count
+            for (int rr = lane; rr < BN; rr += 32) {
+              const int idx = (-jt - 1) * BN + rr;
+              const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
+              for (int a = 0; a < SM::NA; ++a)
+                tma_load_3d(kdst + a * BM * 128 + rr * 128, &tm_kr, &B.k_full[sk], a * 64, f.hk, f.start + pos);
+            }
           }
-          umma_commit(&s_full[grp]);
-          if (j == NK - 1) umma_commit(&q_empty[qb]);
+          if (!mbar_wait(&B.v_empty[sv], ((uint32_t)(g / NSV) & 1) ^ 1, p.err, 14)) { ok = false; break; }
+          if (lane == 0) mbar_arrive_expect_tx(&B.v_full[sv], SM::TILE_BYTES);
+          __syncwarp();
+          if (jt >= 0) {
+            if (lane == 0)
+              for (int a = 0; a < SM::NA; ++a)
+                tma_load_3d(vdst + a * BM * 128, &tm_v, &B.v_full[sv], a * 64, f.hk, f.start + f.kstart + jt * BN);
+          } else {
+            for (int rr = lane; rr < BN; rr += 32) {
+              const int idx = (-jt - 1) * BN + rr;
+              const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
+              for (int a = 0; a < SM::NA; ++a)
+                tma_load_3d(vdst + a * BM * 128 + rr * 128, &tm_vr, &B.v_full[sv], a * 64, f.hk, f.start + pos);
+            }
+          }
         }
-        __syncwarp();
-        ++n_s[grp];
-        return true;
-      };
-      if (!issue_S(0) || (NK > 1 && !issue_S(1))) { *abort_flag = 1; break; }
-      for (int j = 0; j < NK; ++j) {
-        const int gg = g + j, st = gg % NST, grp = j & 1;
-        const bool first = j < 2;
-        // the group releases S_j before P_j is ready: refill its buffer first
-        if (j + 2 < NK && !issue_S(j + 2)) { ok = false; break; }
-        if (first && !mbar_wait(&o_empty[grp], (n_it[grp] & 1) ^ 1, p.err, 25)) { ok = false; break; }
-        if (!mbar_wait(&p_full[grp], n_pv[grp] & 1, p.err, 24)) { ok = false; break; }
-        tc_fence_after();
-        if (elect_one()) {
-          const uint32_t vaddr = sbase + SM::V_OFF + st * SM::TILE_BYTES;
-#pragma unroll
-          for (int ks = 0; ks < BN / 16; ++ks)
-            umma_ts(tbase + COL_O + grp * HD, tbase + COL_P + grp * 64 + ks * 8,
-                    sw128_desc(vaddr + ks * 2048, BM * 128, 1024), p.idesc_pv, (ks > 0 || !first) ? 1u : 0u);
-          umma_commit(&o_full[grp]);
-          umma_commit(&kv_empty[st]);
-        }
-        __syncwarp();
-        ++n_pv[grp];
-        if (first) ++n_it[grp];
       }
-      if (!ok) { *abort_flag = 1; break; }
-      g += NK;
+    } else {
+      // ---------------------------------------------------------------- MMA issuer
+      int g = 0, it = 0;
+      uint32_t ns = 0, npv = 0;
+      bool ok = true;
+      for (int item = item0; item < n_items && ok; item += istride, ++it) {
+        const int sl_i = it % NIS;
+        if (!mbar_wait(&B.it_full[sl_i], (it / NIS) & 1, p.err, 26)) break;
+        const Item f = slots[sl_i].f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.it_empty[sl_i]);
+        const int NK = f.nwt + f.nlt;
+        const int qb = it % NQB;
+        if (!mbar_wait(&B.q_full[qb], (it / NQB) & 1, p.err, 21)) break;
+        const uint32_t qaddr = pbase + SM::Q_OFF + qb * SM::TILE_BYTES;
+        auto issue_S = [&](int t) -> bool {
+          const int gg = g + t, sk = gg % NSK;
+          if (!mbar_wait(&B.k_full[sk], (uint32_t)(gg / NSK) & 1, p.err, 22)) return false;
+          if (!mbar_wait(B.s_empty, (ns & 1) ^ 1, p.err, 23)) return false;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t kaddr = pbase + SM::K_OFF + sk * SM::TILE_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+              const uint32_t koff = (ks >> 2) * BM * 128 + (ks & 3) * 32;
+              umma_ss(tpipe + COL_S, sw128_desc(qaddr + koff, 16, 1024), sw128_desc(kaddr + koff, 16, 1024),
+                      p.idesc_qk, ks > 0 ? 1u : 0u);
+            }
+            umma_commit(B.s_full);
+            umma_commit(&B.k_empty[sk]);
+            if (t == NK - 1) umma_commit(&B.q_empty[qb]);
+          }
+          __syncwarp();
+          ++ns;
+          return true;
+        };
+        if (!issue_S(0)) { ok = false; break; }
+        for (int t = 0; t < NK; ++t) {
+          const int gg = g + t, sv = gg % NSV;
+          // the softmax releases S_t before P_t is ready: refill S first
+          if (t + 1 < NK && !issue_S(t + 1)) { ok = false; break; }
+          if (t == 0 && !mbar_wait(B.o_empty, (it & 1) ^ 1, p.err, 25)) { ok = false; break; }
+          if (!mbar_wait(B.p_full, npv & 1, p.err, 24)) { ok = false; break; }
+          if (!mbar_wait(&B.v_full[sv], (uint32_t)(gg / NSV) & 1, p.err, 27)) { ok = false; break; }
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t vaddr = pbase + SM::V_OFF + sv * SM::TILE_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < BN / 16; ++ks)
+              umma_ts(tpipe + COL_O, tpipe + COL_P + ks * 8, sw128_desc(vaddr + ks * 2048, BM * 128, 1024),
+                      p.idesc_pv, (ks > 0 || t > 0) ? 1u : 0u);
+            umma_commit(B.o_full);
+            umma_commit(&B.v_empty[sv]);
+          }
+          __syncwarp();
+          ++npv;
+        }
+        g += NK;
+      }
     }
-  }  // warps 2, 3: no role
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
-    // ------------------------------------------------------------------ softmax groups
-    const int grp = (warp - 4) >> 2;  // 0: warps 4-7, 1: warps 8-11
+    // ------------------------------------------------------------------ softmax
     const int quad = warp & 3;        // TMEM lane quadrant of this warp
     const int r = quad * 32 + lane;   // query row of the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t tS = tbase + lane_off + COL_S + grp * BN;
-    const uint32_t tP = tbase + lane_off + COL_P + grp * 64;
-    const uint32_t tO = tbase + lane_off + COL_O + grp * HD;
+    const uint32_t tS = tpipe + lane_off + COL_S;
+    const uint32_t tP = tpipe + lane_off + COL_P;
+    const uint32_t tO = tpipe + lane_off + COL_O;
     const float sl = p.scale_log2;
-    uint32_t u = 0, n_items_grp = 0, n_done = 0;
+    const bool bf = (p.idesc_qk >> 7) & 1;
+    uint32_t u = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++n_done) {
-      const Item f = item_info(p, item);
+    int it = 0;
+    for (int item = item0; item < n_items && ok; item += istride, ++it) {
+      const int sl_i = it % NIS;
+      if (!mbar_wait(&B.it_full[sl_i], (it / NIS) & 1, p.err, 36)) break;
+      const Item f = slots[sl_i].f;
+      const int lo = slots[sl_i].lo[r];
+      const int lcnt = slots[sl_i].lcnt[r];
+      mbar_arrive(&B.it_empty[sl_i]);
       const int NK = f.nwt + f.nlt;
       const int i = f.m0 + r;
       const bool vrow = i < f.L;
-      int wi = vrow ? p.w[f.start + i] : 1;
-      wi = wi < 1 ? 1 : wi;
-      const int lo_raw = i - wi + 1;
-      const int lo = lo_raw < 0 ? 0 : lo_raw;
-      const int lim = vrow ? max(0, min(f.L, lo_raw)) : 0;  // landmark p valid iff 0 <= p < lim
-      const int32_t* Pset = p.lmk + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk;
       const float* Bset = p.lmk_bias ? p.lmk_bias + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk : nullptr;
-      // landmark sets are ascending with -1 padding last: as unsigned values they are
-      // non-decreasing, so the valid landmarks of this row (0 <= p < lim) are the first
-      // lcnt entries
-      int lcnt = 0;
-      {
-        int lo_i = 0, hi_i = p.k_lmk;
-        while (lo_i < hi_i) {
-          const int mid = (lo_i + hi_i) >> 1;
-          if ((unsigned)__ldg(Pset + mid) < (unsigned)lim) lo_i = mid + 1;
-          else hi_i = mid;
-        }
-        lcnt = lo_i;
-      }
       float m_acc = -INFINITY, l = 0.0f;  // running max (log2 units, stale by < 2^8) and row sum
-      bool have = false;
-      for (int j = grp; j < NK; j += 2) {
-        if (!mbar_wait(&s_full[grp], u & 1, p.err, 32)) { ok = false; break; }
+      for (int t = 0; t < NK; ++t) {
+        if (!mbar_wait(B.s_full, u & 1, p.err, 32)) { ok = false; break; }
         tc_fence_after();
         // the whole S row in registers: one TMEM round trip, then the buffer is released
         float x[BN];
@@ -399,12 +468,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&s_empty[grp]);
+        mbar_arrive(B.s_empty);
         // valid columns of this row in the tile: [a, b] (window: lo..i; landmarks: the
-        // first lcnt entries of the ascending set, i.e. positions p < lim)
-        const bool is_w = j < f.nwt;
-        const int lt = j - f.nwt;
-        const int kb = f.kstart + j * BN;
+        // first lcnt entries of the ascending set)
+        const int jt = tile_at(f, t);
+        const bool is_w = jt >= 0;
+        const int lt = -jt - 1;
+        const int kb = f.kstart + jt * BN;
         const int a = is_w ? (vrow ? lo - kb : BN) : 0;
         const int b = is_w ? (vrow ? i - kb : -1) : lcnt - 1 - lt * BN;
         if (!is_w && Bset != nullptr) {
@@ -444,9 +514,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // rescale only when the row max grows by more than the threshold
         const bool need = m_tile > m_acc + RESCALE_THRESHOLD;
         const float m_new = need ? m_tile : m_acc;
-        if (have) {
-          // previous P·V of this group done: P buffer free, O may be rescaled
-          if (!mbar_wait(&o_full[grp], (u - 1) & 1, p.err, 33)) { ok = false; break; }
+        if (t > 0) {
+          // previous P·V done: P buffer free, O may be rescaled
+          if (!mbar_wait(B.o_full, (u - 1) & 1, p.err, 33)) { ok = false; break; }
           tc_fence_after();
           if (__any_sync(0xffffffffu, need)) {
             const float fac = need ? ex2_approx(m_acc - m_new) : 1.0f;
@@ -462,14 +532,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tmem_wait_st();
             l *= fac;
           }
-        } else if (need) {
-          l = 0.0f;  // first tile of the group in this item: O is written, not accumulated
         }
         m_acc = m_new;
         const float mu = (m_acc == -INFINITY) ? 0.0f : m_acc;
         const uint64_t sl2 = pk2(sl, sl), nmu2 = pk2(-mu, -mu);
         uint64_t s0 = pk2(0.f, 0.f), s1 = s0;
-        const bool bf = (p.idesc_qk >> 7) & 1;
         // probabilities, row sum, P -> TMEM as 16-bit pairs. Per 32-column chunk the warp
         // masks only when some lane keeps part of it, and skips the exponentials when no
         // lane keeps any of it.
@@ -507,50 +574,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         l += ss.x + ss.y;
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[grp]);
-        have = true;
+        mbar_arrive(B.p_full);
         ++u;
       }
       if (!ok) break;
-      // this group's O of the item, loaded once its last P·V is done
+      // the item's O, once its last P·V is done
+      if (!mbar_wait(B.o_full, (u - 1) & 1, p.err, 34)) { ok = false; break; }
+      tc_fence_after();
       float acc[HD];
-      if (have) {
-        if (!mbar_wait(&o_full[grp], (u - 1) & 1, p.err, 34)) { ok = false; break; }
-        tc_fence_after();
 #pragma unroll
-        for (int cc = 0; cc < HD / 32; ++cc) {
-          uint32_t* orr = reinterpret_cast<uint32_t*>(acc + cc * 32);
-          DSALT_TMEM_LD32(tO + cc * 32, orr);
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&o_empty[grp]);
-        ++n_items_grp;
-      } else {
-#pragma unroll
-        for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t* orr = reinterpret_cast<uint32_t*>(acc + cc * 32);
+        DSALT_TMEM_LD32(tO + cc * 32, orr);
       }
-      if (grp == 1) {
-        if (!mbar_wait(mrg_empty, (n_done & 1) ^ 1, p.err, 35)) { ok = false; break; }
-        mrg[r] = m_acc;
-        mrg[BM + r] = l;
-#pragma unroll
-        for (int d = 0; d < HD; ++d) mrg[(2 + d) * BM + r] = acc[d];
-        mbar_arrive(mrg_full);
-        continue;
-      }
-      if (!mbar_wait(mrg_full, n_done & 1, p.err, 36)) { ok = false; break; }
-      const float mB = mrg[r], lB = mrg[BM + r];
-      const float m = fmaxf(m_acc, mB);
-      const float fA = (m_acc == -INFINITY) ? 0.0f : ex2_approx(m_acc - m);
-      const float fB = (mB == -INFINITY) ? 0.0f : ex2_approx(mB - m);
-#pragma unroll
-      for (int d = 0; d < HD; ++d) acc[d] = acc[d] * fA + mrg[(2 + d) * BM + r] * fB;
-      const float lt = l * fA + lB * fB;
-      mbar_arrive(mrg_empty);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(B.o_empty);
       if (vrow) {
-        const bool good = lt > 1e-9f;
-        const float inv = good ? 1.0f / lt : 0.0f;
+        const bool good = l > 1e-9f;
+        const float inv = good ? 1.0f / l : 0.0f;
         const int64_t row = (int64_t)(f.start + i);
         if (p.out_dtype == DSALT_F32) {
           float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (row * p.H + f.h) * HD);
@@ -559,21 +601,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             o[d / 4] = make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
         } else {
           uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + (row * p.H + f.h) * HD);
-          const bool bf = p.out_dtype == DSALT_BF16;
+          const bool bo = p.out_dtype == DSALT_BF16;
 #pragma unroll
           for (int d = 0; d < HD; d += 8) {
             uint4 q4;
-            q4.x = bf ? pack_bf16x2(acc[d] * inv, acc[d + 1] * inv) : pack_f16x2(acc[d] * inv, acc[d + 1] * inv);
-            q4.y = bf ? pack_bf16x2(acc[d + 2] * inv, acc[d + 3] * inv) : pack_f16x2(acc[d + 2] * inv, acc[d + 3] * inv);
-            q4.z = bf ? pack_bf16x2(acc[d + 4] * inv, acc[d + 5] * inv) : pack_f16x2(acc[d + 4] * inv, acc[d + 5] * inv);
-            q4.w = bf ? pack_bf16x2(acc[d + 6] * inv, acc[d + 7] * inv) : pack_f16x2(acc[d + 6] * inv, acc[d + 7] * inv);
+            q4.x = bo ? pack_bf16x2(acc[d] * inv, acc[d + 1] * inv) : pack_f16x2(acc[d] * inv, acc[d + 1] * inv);
+            q4.y = bo ? pack_bf16x2(acc[d + 2] * inv, acc[d + 3] * inv) : pack_f16x2(acc[d + 2] * inv, acc[d + 3] * inv);
+            q4.z = bo ? pack_bf16x2(acc[d + 4] * inv, acc[d + 5] * inv) : pack_f16x2(acc[d + 4] * inv, acc[d + 5] * inv);
+            q4.w = bo ? pack_bf16x2(acc[d + 6] * inv, acc[d + 7] * inv) : pack_f16x2(acc[d + 6] * inv, acc[d + 7] * inv);
             o[d / 8] = q4;
           }
         }
-        if (p.lse) p.lse[row * p.H + f.h] = good ? (m + log2f(lt)) * 0.6931471805599453f : -INFINITY;
+        const float mm = (m_acc == -INFINITY) ? 0.0f : m_acc;
+        if (p.lse) p.lse[row * p.H + f.h] = good ? (mm + log2f(l)) * 0.6931471805599453f : -INFINITY;
       }
     }
-    if (!ok) *abort_flag = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -600,12 +642,13 @@ static EncodeTiledFn get_encode() {
   return fn;
 }
 
-static int make_map(CUtensorMap* m, const void* base, int dtype, int HD, int heads, int64_t T, int64_t row_stride) {
+static int make_map(CUtensorMap* m, const void* base, int dtype, int HD, int heads, int64_t T, int64_t row_stride,
+                    uint32_t box_rows = BM) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return fail(DSALT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)heads, (cuuint64_t)T};
   const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)row_stride * 2};
-  const cuuint32_t box[3] = {64, 1, (cuuint32_t)BM};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, dtype == DSALT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -627,11 +670,13 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15 || (q_stride * 2) % 16 ||
       (kv_stride * 2) % 16)
     return fail(DSALT_ERR_INVALID, "attention: q/k/v/out must be 16-byte aligned with 16-byte row strides");
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mkr, mvr;
   int rc;
   if ((rc = make_map(&mq, q, dtype, HD, H, T, q_stride))) return rc;
   if ((rc = make_map(&mk, k, dtype, HD, Hkv, T, kv_stride))) return rc;
   if ((rc = make_map(&mv, v, dtype, HD, Hkv, T, kv_stride))) return rc;
+  if ((rc = make_map(&mkr, k, dtype, HD, Hkv, T, kv_stride, 1))) return rc;  // one-row boxes: landmark gather
+  if ((rc = make_map(&mvr, v, dtype, HD, Hkv, T, kv_stride, 1))) return rc;
   if ((rc = launch_chunk_table(cu, n_seqs, BM, tile_base, stream))) return rc;
   if (lmk_block > 0 && (rc = launch_chunk_table(cu, n_seqs, lmk_block, set_base, stream))) return rc;
   Params p{};
@@ -662,14 +707,15 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int64_t max_items = (T / BM + n_seqs) * (int64_t)H;
-  const int grid = (int)(max_items < nsm ? max_items : nsm);
+  const int64_t want = (max_items + NPIPE - 1) / NPIPE;
+  const int grid = (int)(want < nsm ? want : nsm);
   if (grid <= 0) return DSALT_OK;
   const size_t smem = Smem<64>::BYTES + 1024;
   if ((rc = check_cuda(cudaFuncSetAttribute(attn_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)smem),
                        "attention smem attr")))
     return rc;
-  attn_fwd_tc_kernel<64><<<grid, NTHREADS, smem, stream>>>(mq, mk, mv, p);
+  attn_fwd_tc_kernel<64><<<grid, NTHREADS, smem, stream>>>(mq, mk, mv, mkr, mvr, p);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 
