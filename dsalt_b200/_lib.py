@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "_lib", "libdsalt_b200.so")
 
 F32, BF16, F16 = 0, 1, 2
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_DEVICE = range(6)
+NOALLOC_MAX_SEQS = 4096  # DSALT_NOALLOC_MAX_SEQS
 SELECT_GLOBAL, SELECT_BLOCK_CAUSAL = 0, 1
 NORM_F32, NORM_INPUT = 0, 1
 
@@ -35,6 +36,8 @@ SIGNATURES = {
     "dsalt_attention_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I]),
     "dsalt_attention_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P, _I, _I, _P, _I, _I,
                                  _P, _I, _P, _P, _SZ, _P]),
+    "dsalt_attention_fwd_noalloc": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P, _I, _I, _P, _I,
+                                         _I, _P, _I, _P, _P]),
     "dsalt_core_workspace_bytes": (_SZ, [_I, _I64, _I, _I, _I, _I, _I, _I, _I]),
     "dsalt_core_forward": (_I, [_I, _P, _I, _I, _I64, _P, _P, _I, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _I,
                                 _I64, _I64, _I, _I, _P, _I, _I64, _I, _P, _I, _P, _P, _P, _SZ, _P]),

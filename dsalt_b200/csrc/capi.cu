@@ -69,6 +69,26 @@ int* device_status_ptr() {
   return ptrs[dev];
 }
 
+// Scratch of dsalt_attention_fwd_noalloc: the query-tile and landmark-set tables for up
+// to DSALT_NOALLOC_MAX_SEQS sequences, laid out as dsalt_attention_fwd carves its
+// workspace (two 256-byte aligned tables of n_seqs + 1 int32).
+constexpr size_t NOALLOC_TABLE_BYTES = ((DSALT_NOALLOC_MAX_SEQS + 1) * sizeof(int32_t) + 255) & ~(size_t)255;
+static __device__ __align__(256) int32_t g_noalloc_scratch[2 * NOALLOC_TABLE_BYTES / sizeof(int32_t)];
+
+static void* noalloc_scratch_ptr() {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
 static bool valid_dtype(int dt) { return dt == DSALT_F32 || dt == DSALT_BF16 || dt == DSALT_F16; }
 static inline size_t a256(size_t v) { return (v + 255) & ~(size_t)255; }
 
@@ -160,6 +180,30 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
   return launch_attn_tc(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
                         lmk_block, cu_seqlens, n_seqs, set_base, tile_base, out, out_dtype, lse, device_status_ptr(),
                         s);
+}
+
+// Callers without a device allocator (bindings that hold only the caller's pointers,
+// serving loops whose pool may not grow) get the attention forward with its scratch in
+// g_noalloc_scratch. Overlapping calls on one device share that array and race.
+int dsalt_attention_fwd_noalloc(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads,
+                                int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, const int32_t* w,
+                                const int32_t* lmk, const float* lmk_bias, int k_lmk, int lmk_block,
+                                const int32_t* cu_seqlens, int n_seqs, int max_seqlen, void* out, int out_dtype,
+                                float* lse, void* stream) {
+  if (n_seqs > DSALT_NOALLOC_MAX_SEQS)
+    return fail(DSALT_ERR_UNSUPPORTED,
+                "attention (no-alloc): n_seqs %d above the static scratch limit %d; use dsalt_attention_fwd with a "
+                "workspace",
+                n_seqs, DSALT_NOALLOC_MAX_SEQS);
+  const size_t need = dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k_lmk, lmk_block);
+  if (need > sizeof(g_noalloc_scratch))
+    return fail(DSALT_ERR_UNSUPPORTED, "attention (no-alloc): scratch %zu above %zu", need,
+                sizeof(g_noalloc_scratch));
+  void* scratch = noalloc_scratch_ptr();
+  if (!scratch) return fail(DSALT_ERR_CUDA, "attention (no-alloc): scratch address unavailable");
+  return dsalt_attention_fwd(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
+                             lmk_block, cu_seqlens, n_seqs, max_seqlen, out, out_dtype, lse, scratch,
+                             sizeof(g_noalloc_scratch), stream);
 }
 
 size_t dsalt_core_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv,
