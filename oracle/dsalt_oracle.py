@@ -32,7 +32,7 @@ Floating-point contract (what "bit-exact" means for the integer outputs):
   is returned sorted by position with ``-1`` padding.
 * The bf16 window chain uses CUDA's fp32 sigmoid ``1/(1+expf(-x))``; for the three bf16
   logits whose bf16 sigmoid depends on the last bit of ``expf`` the value measured on a
-  B200 is used (``tests/golden/sigmoid_bf16_cuda.json``) when it is available, and those
+  B200 is used (``tests/golden/sigmoid_bf16_cuda.npz``) when it is available, and those
   logits are otherwise reported as ambiguous.
 
 Parity of this oracle against the reference is pinned by ``tests/golden/`` (fixtures
@@ -40,7 +40,6 @@ produced by running the reference itself on CPU, see ``tests/golden/make_golden.
 """
 from __future__ import annotations
 
-import json
 import math
 import os
 from dataclasses import dataclass
@@ -51,7 +50,7 @@ F32 = np.float32
 F64 = np.float64
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-_SIGMOID_TABLE_PATH = os.path.join(os.path.dirname(_HERE), "tests", "golden", "sigmoid_bf16_cuda.json")
+_SIGMOID_TABLE_PATH = os.path.join(os.path.dirname(_HERE), "tests", "golden", "sigmoid_bf16_cuda.npz")
 
 
 # --------------------------------------------------------------------------- #
@@ -115,9 +114,8 @@ def _f64_to_bf16(acc: np.ndarray) -> np.ndarray:
 
 def _load_sigmoid_table() -> dict:
     if os.path.exists(_SIGMOID_TABLE_PATH):
-        with open(_SIGMOID_TABLE_PATH) as fh:
-            d = json.load(fh)
-        return {int(k): int(v) for k, v in d.get("cuda_sigmoid_bf16_bits", {}).items()}
+        d = np.load(_SIGMOID_TABLE_PATH)
+        return {int(k): int(v) for k, v in zip(d["logit_bits"].tolist(), d["sigmoid_bits"].tolist())}
     return {}
 
 

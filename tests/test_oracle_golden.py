@@ -200,3 +200,16 @@ def test_masked_sdpa_port_matches_reference_fallback():
     mod = torch.nn.functional.linear(torch.as_tensor(o).reshape(x.shape[0], -1), params["out_proj.weight"])
     err = (mod.numpy()[d["rows"]] - d["fallback_mod_rows"]).__abs__().max()
     assert err <= 1e-5, err
+
+
+def test_sigmoid_table_covers_every_ambiguous_logit():
+    """The B200 measurement (``tests/golden/make_sigmoid_table.py``) lists exactly the bf16
+    logits whose sigmoid rounding the oracle cannot decide, so no width stays ambiguous."""
+    d = np.load(os.path.join(GOLDEN, "sigmoid_bf16_cuda.npz"))
+    bits = np.arange(65536, dtype=np.uint32)
+    vals = O.bf16_bits_to_f32(bits)
+    fin = np.isfinite(vals)
+    amb = O.sigmoid_ambiguous_f32(vals[fin], O._sigmoid_exact(vals[fin]))
+    assert set(bits[fin][amb].tolist()) == set(d["logit_bits"].astype(np.uint32).tolist())
+    _, still = O.sigmoid_bf16(O.bf16_bits_to_f32(d["logit_bits"].astype(np.uint32)))
+    assert not np.any(still)
