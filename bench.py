@@ -46,6 +46,19 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def profiled_traffic(T):
+    """DRAM bytes (read + write) of one attention launch at this sequence length, from
+    the committed ncu summary (a line ``dram_bytes_per_launch[L=<T>]: <bytes>``)."""
+    import re
+    path = os.path.join(ROOT, "profiles", "attn_fwd_tc.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch\[L=%d\]:\s*([0-9.eE+]+)" % T, txt)
+    return float(m.group(1)) if m else None
+
+
 def make_inputs(dev, seed=0):
     from dsalt_b200.module import apply_rotary_emb, build_rope_cache
     T, H, D, dm = CFG["L"], CFG["H"], CFG["D"], CFG["dm"]
@@ -142,33 +155,39 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-def cpu_baseline(x, gw, gb, alpha, q, k, v, budget_s=12.0):
-    """The reference's block-causal CPU path on a sample of blocks spread along L."""
-    from dsalt_b200 import ops
+def _cpu_port(x, gw, gb, alpha, q, k, v):
     from oracle.cpu_baseline import BlockCausalCPU
-    T, B = CFG["L"], CFG["block"]
-    w, xn, vn = ops.window_signals(x, gw, gb, CFG["n_min"], CFG["n_max"], v.view(T, -1), CFG["D"])
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    base = BlockCausalCPU(q.float().cpu(), k.float().cpu(), v.float().cpu(), w.cpu(), xn.cpu(), vn.cpu(),
-                          alpha.cpu(), CFG["k"], B)
-    nb = T // B
-    base.run_block(nb // 2)  # warm-up
-    order = [int(round(i * (nb - 1) / 31)) for i in range(32)]
-    done, tok, spent = [], 0, 0.0
-    for b in order:
-        t, dt = base.time_sample([b])
-        done.append(b)
+    base = BlockCausalCPU(x.cpu(), gw.cpu(), gb.cpu(), CFG["n_min"], CFG["n_max"], q.cpu(), k.cpu(), v.cpu(),
+                          alpha.cpu(), CFG["k"], CFG["block"])
+    return base, cores
+
+
+def cpu_baseline(x, gw, gb, alpha, q, k, v, min_s=10.0):
+    """The reference's block-causal CPU path over the whole L=131072 sequence (signals,
+    widths, prefix statistics, selection and attention of all 256 blocks), repeated until
+    at least ``min_s`` seconds of CPU work have been timed."""
+    base, cores = _cpu_port(x, gw, gb, alpha, q, k, v)
+    nb = -(-CFG["L"] // CFG["block"])
+    base.time_blocks(0, 2)  # warm-up
+    tok, spent, passes = 0, 0.0, 0
+    while spent < min_s:
+        t, dt = base.time_blocks(0, nb)
         tok += t
         spent += dt
-        if spent > budget_s:
-            break
+        passes += 1
     return {"value": tok / spent, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{len(done)} of {nb} 512-query blocks spread over L=131072 (select + attention, fp32 "
-                      f"torch CPU restatement of the reference's block-causal path), {spent:.1f} s"}
+            "sample": f"{passes} full pass(es) over L={CFG['L']} (signals, widths, block-causal selection and "
+                      f"attention of all {nb} 512-query blocks; fp32 torch CPU restatement of the reference's "
+                      f"path), {spent:.1f} s"}
 
 
 def run_reference(args):
+    """--impl reference: the reference's CPU path (restated, see oracle/cpu_baseline.py) on
+    this host's cores. A step streams the next run of consecutive 512-query blocks of the
+    same L=131072 workload, sized so that all warm-up and timed steps take about three
+    minutes in total; the value is tokens over time summed over the timed steps."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -177,19 +196,30 @@ def run_reference(args):
         print(json.dumps({"impl": "reference", "unavailable": "no CUDA device to build the synthetic inputs"}))
         return
     x, gw, gb, alpha, q, k, v = make_inputs(dev)
-    vals = []
-    base = None
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(x, gw, gb, alpha, q, k, v, budget_s=6.0 if i >= args.warmup else 2.0)
+    base, cores = _cpu_port(x, gw, gb, alpha, q, k, v)
+    nb = -(-CFG["L"] // CFG["block"])
+    t, dt = base.time_blocks(0, 4)  # calibration: seconds per block
+    per_block = dt / 4
+    n_steps = args.warmup + args.steps
+    bps = max(1, min(nb, int(min(3.0, 180.0 / n_steps) / per_block)))
+    nxt, tok, spent = 4, 0, 0.0
+    for i in range(n_steps):
+        if nxt >= nb:
+            nxt = 0
+        b1 = min(nb, nxt + bps)
+        t, dt = base.time_blocks(nxt, b1)
+        nxt = b1
         if i >= args.warmup:
-            vals.append(r["value"])
-            base = r
-    value = statistics.median(vals)
+            tok += t
+            spent += dt
+    value = tok / spent
+    sample = (f"{args.steps} timed steps of {bps} consecutive 512-query blocks each, streamed through "
+              f"L={CFG['L']} (signals, widths, selection, attention), {spent:.1f} s")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": CFG["L"] / value * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": spent / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": CFG["workload"], "where": "host CPU cores"},
-            "cpu_baseline": {**base, "value": value},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -202,7 +232,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seq-len", type=int, default=CFG["L"],
+                    help="sequence length (131072 is the benchmark; shorter ones for profiler captures)")
     args = ap.parse_args()
+    if args.seq_len != CFG["L"]:
+        CFG["L"] = args.seq_len
+        CFG["workload"] = CFG["workload"].replace("L131072", f"L{args.seq_len}")
     if args.impl == "reference":
         return run_reference(args)
     args.warmup = max(args.warmup, 3)
@@ -256,13 +291,7 @@ def main():
     att_bytes = 4 * T * H * D * 2  # q, k, v read once + output written once (bf16)
     hbm, src = peaks()
     achieved = att_bytes / (att_ms / 1e3) / 1e9
-    traffic = None
-    prof = os.path.join(ROOT, "profiles", "attn_fwd_tc_L131072.json")
-    if os.path.exists(prof):
-        try:
-            traffic = json.load(open(prof)).get("dram_bytes_per_launch")
-        except Exception:
-            traffic = None
+    traffic = profiled_traffic(T)
 
     # end to end through the C-ABI call with host buffers
     xh = x.cpu().pin_memory()
@@ -299,7 +328,8 @@ def main():
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": CFG["workload"], "L": T, "heads": H, "head_dim": D, "d_model": CFG["dm"],
                            "k_lmk": k, "block": B, "n_min": CFG["n_min"], "n_max": CFG["n_max"],
-                           "selection": "block_causal", "l2": "inputs larger than L2 (1.3 GB per step)",
+                           "selection": "block_causal",
+                           "l2": f"inputs larger than L2 ({(T * CFG['dm'] * 2 + 3 * T * H * D * 2) / 1e9:.2f} GB per step)",
                            "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
                 "clocks": clk.summary(), "device_status": status,
                 "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(HERE, "_lib", "libdsalt_b200.so")
 F32, BF16, F16 = 0, 1, 2
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_DEVICE = range(6)
 NOALLOC_MAX_SEQS = 4096  # DSALT_NOALLOC_MAX_SEQS
+NOALLOC_MAX_TOKENS = 1048576  # DSALT_NOALLOC_MAX_TOKENS
 SELECT_GLOBAL, SELECT_BLOCK_CAUSAL = 0, 1
 NORM_F32, NORM_INPUT = 0, 1
 

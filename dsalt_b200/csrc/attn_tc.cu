@@ -9,13 +9,14 @@
 //
 // Work item = (128-query tile, head); persistent CTAs, one per SM. Per item the key
 // axis is a band of 128-key window tiles ending at the tile's last row and reaching back
-// to max(0, m0 − max_w + 1), plus ceil(k/128) landmark tiles; the diagonal tile goes
-// first, then the landmark tiles, then the other window tiles. Each CTA runs two
-// independent pipelines (A, B) on alternate items; a pipeline is
+// to max(0, m0 − max_w + 1), plus ceil(k/128) landmark tiles; the window tiles go from
+// the diagonal one leftwards, then the landmark tiles. Each CTA runs two independent
+// pipelines (A, B) on alternate items; a pipeline is
 //   a producer warp   TMA (no multicast) of the Q tile and the K/V window tiles into a
-//                     3-stage K ring and a 2-stage V ring; landmark K/V rows gathered by
-//                     one-row TMA boxes into the same rings (replaces _build_landmark_kv,
-//                     selectors.py:137-159);
+//                     3-stage K ring and a 2-stage V ring; landmark K/V rows gathered with
+//                     cp.async into the same rings (replaces _build_landmark_kv,
+//                     selectors.py:137-159); it fills the next item's description slot
+//                     while the current item's last gather is in flight;
 //   an MMA warp       one thread issues S = Q·Kᵀ (SS form) into TMEM and O += P·V (TS
 //                     form: P read from TMEM, V from smem) into a TMEM accumulator;
 //   4 softmax warps   row r ↔ TMEM lane r: the S row is read once into registers,
@@ -68,6 +69,7 @@ struct Params {
   int n_seqs;
   const int32_t* set_base;
   const int32_t* tile_base;
+  const int4* plan;  // per query tile: {start, L, m0, set}, {kstart, nwt, -, -}
   float scale_log2;  // log2(e) / sqrt(head_dim)
   float inv_scale;   // sqrt(head_dim): landmark bias in raw-logit units
   uint32_t idesc_qk, idesc_pv;
@@ -78,7 +80,7 @@ struct Params {
 };
 
 struct Item {
-  int s, start, L, m0, h, hk, kstart, nwt, nlt, set, n_sets;
+  int start, L, m0, h, hk, kstart, nwt, nlt, set, n_sets;
 };
 
 __device__ __forceinline__ int find_seq(const int32_t* base, int n, int idx) {
@@ -91,42 +93,54 @@ __device__ __forceinline__ int find_seq(const int32_t* base, int n, int idx) {
   return lo;
 }
 
-// warp-collective: every lane returns the same description of work item `item`
-__device__ __forceinline__ Item item_info(const Params& p, int item) {
+// Per query tile (one warp each): the sequence it lies in and the band of key tiles its
+// window needs. Window tiles end at the tile's last row, so that the last one holds
+// every row's diagonal key; the first may start before the sequence (those keys are
+// masked). Replaces _build_seq_block_map (selectors.py:37-67).
+__global__ void tile_plan_kernel(const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ tile_base,
+                                 const int32_t* __restrict__ set_base, int lmk_block, const int32_t* __restrict__ w,
+                                 int4* __restrict__ plan) {
+  const int tile = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (tile >= tile_base[n_seqs]) return;
+  const int s = find_seq(tile_base, n_seqs, tile);
+  const int start = cu[s], L = cu[s + 1] - start;
+  const int m0 = (tile - tile_base[s]) * BM;
+  int wm = 1;
+  for (int r = lane; r < BM; r += 32)
+    if (m0 + r < L) wm = max(wm, __ldg(w + start + m0 + r));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+  const int hi = min(m0 + BM - 1, L - 1);
+  const int kmin = max(0, m0 - wm + 1);
+  const int nwt = (hi - kmin + BN) / BN;
+  if (lane == 0) {
+    plan[2 * tile] = make_int4(start, L, m0, lmk_block ? set_base[s] + m0 / lmk_block : s);
+    plan[2 * tile + 1] = make_int4(hi + 1 - nwt * BN, nwt, 0, 0);
+  }
+}
+
+__device__ __forceinline__ Item make_item(const Params& p, int item, int4 a, int4 b, int n_sets) {
   Item f;
   const int tile = item / p.H;
   f.h = item - tile * p.H;
   f.hk = f.h / (p.H / p.Hkv);
-  f.s = find_seq(p.tile_base, p.n_seqs, tile);
-  f.start = p.cu[f.s];
-  f.L = p.cu[f.s + 1] - f.start;
-  f.m0 = (tile - p.tile_base[f.s]) * BM;
-  int wm = 1;
-  for (int r = threadIdx.x & 31; r < BM; r += 32) {
-    const int i = f.m0 + r;
-    if (i < f.L) wm = max(wm, p.w[f.start + i]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, o));
-  // window tiles end at the tile's last row, so that the last one holds every row's
-  // diagonal key; the first may start before the sequence (those keys are masked)
-  const int hi = min(f.m0 + BM - 1, f.L - 1);
-  const int kmin = max(0, f.m0 - wm + 1);
-  f.nwt = (hi - kmin + BN) / BN;
-  f.kstart = hi + 1 - f.nwt * BN;
+  f.start = a.x;
+  f.L = a.y;
+  f.m0 = a.z;
+  f.set = a.w;
+  f.kstart = b.x;
+  f.nwt = b.y;
   f.nlt = (p.k_lmk + BN - 1) / BN;
-  f.n_sets = p.lmk_block ? p.set_base[p.n_seqs] : p.n_seqs;
-  f.set = p.lmk_block ? p.set_base[f.s] + f.m0 / p.lmk_block : f.s;
+  f.n_sets = n_sets;
   return f;
 }
 
-// Processing order of an item's key tiles: the diagonal window tile first (every valid
-// row gets a finite running max at once), then the landmark tiles, then the remaining
-// window tiles right to left. Returns the window-tile index, or -1 - (landmark tile).
+// Processing order of an item's key tiles: the window tiles from the diagonal one leftwards
+// (every valid row gets a finite running max on the first tile), then the landmark tiles.
+// Returns the window-tile index, or -1 - (landmark tile).
 __device__ __forceinline__ int tile_at(const Item& f, int t) {
-  if (t == 0) return f.nwt - 1;
-  if (t <= f.nlt) return -t;
-  return f.nwt - 1 - (t - f.nlt);
+  return t < f.nwt ? f.nwt - 1 - t : -1 - (t - f.nwt);
 }
 
 template <int HD>
@@ -137,8 +151,8 @@ struct Smem {
   static constexpr uint32_t Q_OFF = 0;                     // + pipe * PIPE_BYTES
   static constexpr uint32_t K_OFF = NQB * TILE_BYTES;
   static constexpr uint32_t V_OFF = K_OFF + NSK * TILE_BYTES;
-  // item slots: description, per-row window start and landmark count, landmark positions
-  static constexpr uint32_t SLOT_BYTES = 64 + 2 * BM * 4 + MAX_LMK * 4;
+  // item slots: description, per-row window widths, landmark positions
+  static constexpr uint32_t SLOT_BYTES = 64 + BM * 4 + MAX_LMK * 4;
   static constexpr uint32_t SLOT_OFF = NPIPE * PIPE_BYTES;  // + (pipe * NIS + slot) * SLOT_BYTES
   static constexpr uint32_t BAR_OFF = SLOT_OFF + NPIPE * NIS * SLOT_BYTES;
   // per pipeline: q_full[NQB] q_empty[NQB] k_full[NSK] k_empty[NSK] v_full[NSV] v_empty[NSV]
@@ -154,6 +168,9 @@ __device__ __forceinline__ uint32_t swz_off(int r, int c) {
   const int atom = c >> 3, cc = c & 7;
   return (uint32_t)(atom * BM * 128 + r * 128 + ((cc ^ (r & 7)) << 4));
 }
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float d;
@@ -203,17 +220,20 @@ struct PipeBars {
 struct Slot {
   Item f;
   int pad[16 - sizeof(Item) / 4];
-  int32_t lo[BM];    // per row: first window key (>= 0), or BM-clamped sentinel for rows past L
-  int32_t lcnt[BM];  // per row: number of landmarks of the set that the row may use
+  int32_t wv[BM];    // per row: window width (0 for rows past the sequence end)
   int32_t pos[MAX_LMK];
 };
 static_assert(sizeof(Item) <= 64, "item description must fit the slot header");
 
-template <int HD>
+// P is packed to the input type: BF = bf16, else fp16
+__device__ __forceinline__ uint32_t pack_p(bool bf, float lo, float hi) {
+  return bf ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+}
+
+template <int HD, bool BF>
 __global__ void __launch_bounds__(NTHREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kr,
-                       const __grid_constant__ CUtensorMap tm_vr, const Params p) {
+                       const __grid_constant__ CUtensorMap tm_v, const Params p) {
   using SM = Smem<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -288,38 +308,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
       }
+      const uint16_t* kg = reinterpret_cast<const uint16_t*>(p.k);
+      const uint16_t* vg = reinterpret_cast<const uint16_t*>(p.v);
+      const int n_sets = p.lmk_block ? __ldg(p.set_base + p.n_seqs) : p.n_seqs;
+      // Publish item `item_n` (the it_n-th of this pipeline) into its slot: the description
+      // from the tile plan (a, b), then the rows' window widths and the landmark positions
+      // by cp.async; the slot is full when the copies have landed.
+      auto publish = [&](int item_n, int it_n, int4 a, int4 b) -> bool {
+        const Item fn = make_item(p, item_n, a, b, n_sets);
+        const int sl = it_n % NIS;
+        if (!mbar_wait(&B.it_empty[sl], ((it_n / NIS) & 1) ^ 1, p.err, 13)) return false;
+        Slot& S = slots[sl];
+        if (lane == 0) S.f = fn;
+        const int32_t* P = p.lmk + ((int64_t)fn.h * fn.n_sets + fn.set) * p.k_lmk;
+        for (int c = lane; c < p.k_lmk; c += 32) cp_async_4(smem_u32(&S.pos[c]), P + c, 4u);
+        for (int r = lane; r < BM; r += 32) {
+          const bool vrow = fn.m0 + r < fn.L;
+          cp_async_4(smem_u32(&S.wv[r]), p.w + fn.start + (vrow ? fn.m0 + r : 0), vrow ? 4u : 0u);
+        }
+        cp_async_mbar_arrive(&B.it_full[sl]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B.it_full[sl]);
+        return true;
+      };
       int g = 0, it = 0;
       bool ok = true;
+      if (item0 < n_items) {
+        const int t0 = item0 / p.H;
+        ok = publish(item0, 0, __ldg(p.plan + 2 * t0), __ldg(p.plan + 2 * t0 + 1));
+      }
       for (int item = item0; item < n_items && ok; item += istride, ++it) {
-        const Item f = item_info(p, item);
-        // publish the item: description, per-row window starts and landmark counts
         const int sl_i = it % NIS;
-        if (!mbar_wait(&B.it_empty[sl_i], ((it / NIS) & 1) ^ 1, p.err, 13)) break;
-        Slot& S = slots[sl_i];
-        if (lane == 0) S.f = f;
-        const int32_t* P = p.lmk + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk;
-        for (int c = lane; c < f.nlt * BN; c += 32) S.pos[c] = c < p.k_lmk ? __ldg(P + c) : -1;
-        __syncwarp();
-        for (int rr = lane; rr < BM; rr += 32) {
-          const int i = f.m0 + rr;
-          const bool vrow = i < f.L;
-          int wi = vrow ? __ldg(p.w + f.start + i) : 1;
-          wi = wi < 1 ? 1 : wi;
-          const int lo_raw = i - wi + 1;
-          S.lo[rr] = vrow ? (lo_raw < 0 ? 0 : lo_raw) : 0x3fffffff;
-          // sets are ascending with -1 last: as unsigned values non-decreasing, so the
-          // landmarks the row may use (0 <= p < min(L, i-w+1)) are a prefix of the set
-          const int lim = vrow ? max(0, min(f.L, lo_raw)) : 0;
-          int a0 = 0, a1 = p.k_lmk;
-          while (a0 < a1) {
-            const int mid = (a0 + a1) >> 1;
-            if ((unsigned)S.pos[mid] < (unsigned)lim) a0 = mid + 1;
-            else a1 = mid;
-          }
-          S.lcnt[rr] = a0;
+        const Slot& S = slots[sl_i];
+        const Item f = S.f;
+        // the next item's plan: loaded now, published after this item's first tile
+        const int item_n = item + istride;
+        const bool has_next = item_n < n_items;
+        int4 an = make_int4(0, 0, 0, 0), bn = an;
+        if (has_next) {
+          an = __ldg(p.plan + 2 * (item_n / p.H));
+          bn = __ldg(p.plan + 2 * (item_n / p.H) + 1);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&B.it_full[sl_i]);
+        bool published = !has_next;
         const int qb = it % NQB;
         if (!mbar_wait(&B.q_empty[qb], ((it / NQB) & 1) ^ 1, p.err, 11)) break;
         if (lane == 0) {
@@ -329,44 +359,76 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         f.start + f.m0);
         }
         const int NK = f.nwt + f.nlt;
+        // the landmark rows are gathered after the window tiles: bring them into L2 now
+        // (scattered 128-byte rows; the gather would otherwise wait on DRAM latency)
+        if (f.nlt > 0) {
+          if (!mbar_wait(&B.it_full[sl_i], (uint32_t)(it / NIS) & 1, p.err, 15)) break;
+          for (int c = lane; c < p.k_lmk; c += 32) {
+            const int pos = S.pos[c];
+            if (pos >= 0) {
+              const int64_t off = (int64_t)(f.start + pos) * p.kv_stride + (int64_t)f.hk * HD;
+              prefetch_l2(kg + off);
+              prefetch_l2(vg + off);
+            }
+          }
+        }
         for (int t = 0; t < NK; ++t, ++g) {
+          if (t == 1 && !published) {
+            if (!publish(item_n, it + 1, an, bn)) { ok = false; break; }
+            published = true;
+          }
           const int jt = tile_at(f, t);
           const int sk = g % NSK, sv = g % NSV;
           const uint32_t kdst = pbase + SM::K_OFF + sk * SM::TILE_BYTES;
           const uint32_t vdst = pbase + SM::V_OFF + sv * SM::TILE_BYTES;
-          if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
-          if (lane == 0) mbar_arrive_expect_tx(&B.k_full[sk], SM::TILE_BYTES);
-          __syncwarp();
           if (jt >= 0) {
-            if (lane == 0)
-              for (int a = 0; a < SM::NA; ++a)
-                tma_load_3d(kdst + a * BM * 128, &tm_k, &B.k_full[sk], a * 64, f.hk, f.start + f.kstart + jt * BN);
-          } else {
-            // landmark rows, one-row TMA boxes; unused slots read row start-1 (or past the
-            // end, zero-filled): those columns are masked by the row's landmark count
-            for (int rr = lane; rr < BN; rr += 32) {
-              const int idx = (-jt - 1) * BN + rr;
-              const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
-              for (int a = 0; a < SM::NA; ++a)
-                tma_load_3d(kdst + a * BM * 128 + rr * 128, &tm_kr, &B.k_full[sk], a * 64, f.hk, f.start + pos);
+            const int row = f.start + f.kstart + jt * BN;
+            if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&B.k_full[sk], SM::TILE_BYTES);
+              for (int a = 0; a < SM::NA; ++a) tma_load_3d(kdst + a * BM * 128, &tm_k, &B.k_full[sk], a * 64, f.hk, row);
             }
-          }
-          if (!mbar_wait(&B.v_empty[sv], ((uint32_t)(g / NSV) & 1) ^ 1, p.err, 14)) { ok = false; break; }
-          if (lane == 0) mbar_arrive_expect_tx(&B.v_full[sv], SM::TILE_BYTES);
-          __syncwarp();
-          if (jt >= 0) {
-            if (lane == 0)
-              for (int a = 0; a < SM::NA; ++a)
-                tma_load_3d(vdst + a * BM * 128, &tm_v, &B.v_full[sv], a * 64, f.hk, f.start + f.kstart + jt * BN);
+            if (!mbar_wait(&B.v_empty[sv], ((uint32_t)(g / NSV) & 1) ^ 1, p.err, 14)) { ok = false; break; }
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&B.v_full[sv], SM::TILE_BYTES);
+              for (int a = 0; a < SM::NA; ++a) tma_load_3d(vdst + a * BM * 128, &tm_v, &B.v_full[sv], a * 64, f.hk, row);
+            }
           } else {
-            for (int rr = lane; rr < BN; rr += 32) {
-              const int idx = (-jt - 1) * BN + rr;
-              const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
-              for (int a = 0; a < SM::NA; ++a)
-                tma_load_3d(vdst + a * BM * 128 + rr * 128, &tm_vr, &B.v_full[sv], a * 64, f.hk, f.start + pos);
+            // landmark rows (replaces _build_landmark_kv): 16-byte cp.async by all lanes into
+            // the swizzled tiles, four rows per instruction; empty slots are zero-filled
+            // (their columns are masked by the row's landmark count, and zeros keep P·V
+            // finite). The positions come from this item's slot.
+            const int lt = -jt - 1;
+            if (!mbar_wait(&B.it_full[sl_i], (uint32_t)(it / NIS) & 1, p.err, 15)) { ok = false; break; }
+            if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
+            if (!mbar_wait(&B.v_empty[sv], ((uint32_t)(g / NSV) & 1) ^ 1, p.err, 14)) { ok = false; break; }
+            constexpr int CPR = HD / 8;     // 16-byte chunks per row
+            constexpr int RPI = 32 / CPR;   // rows per instruction
+            const int c = lane % CPR, rsub = lane / CPR;
+            const int64_t head_off = (int64_t)f.hk * HD + c * 8;
+            for (int rb = 0; rb < BN; rb += 32) {
+#pragma unroll
+              for (int j = 0; j < 32 / RPI; ++j) {
+                const int rr = j * RPI + rsub;
+                const int idx = lt * BN + rb + rr;
+                const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
+                const int64_t off = (int64_t)(f.start + (pos < 0 ? 0 : pos)) * p.kv_stride + head_off;
+                const uint32_t so = swz_off<HD>(rb + rr, c);
+                const uint32_t nb = pos < 0 ? 0u : 16u;
+                cp_async_16(kdst + so, kg + off, nb);
+                cp_async_16(vdst + so, vg + off, nb);
+              }
+            }
+            cp_async_wait_all();
+            fence_proxy_async_smem();  // generic-proxy writes -> tensor-core (async proxy) reads
+            __syncwarp();
+            if (lane == 0) {
+              mbar_arrive(&B.k_full[sk]);
+              mbar_arrive(&B.v_full[sv]);
             }
           }
         }
+        if (ok && !published && !publish(item_n, it + 1, an, bn)) ok = false;
       }
     } else {
       // ---------------------------------------------------------------- MMA issuer
@@ -438,22 +500,38 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t tP = tpipe + lane_off + COL_P;
     const uint32_t tO = tpipe + lane_off + COL_O;
     const float sl = p.scale_log2;
-    const bool bf = (p.idesc_qk >> 7) & 1;
+    constexpr bool bf = BF;
     uint32_t u = 0;
     bool ok = true;
     int it = 0;
     for (int item = item0; item < n_items && ok; item += istride, ++it) {
       const int sl_i = it % NIS;
       if (!mbar_wait(&B.it_full[sl_i], (it / NIS) & 1, p.err, 36)) break;
-      const Item f = slots[sl_i].f;
-      const int lo = slots[sl_i].lo[r];
-      const int lcnt = slots[sl_i].lcnt[r];
-      mbar_arrive(&B.it_empty[sl_i]);
-      const int NK = f.nwt + f.nlt;
+      const Slot& S = slots[sl_i];
+      const Item f = S.f;
       const int i = f.m0 + r;
       const bool vrow = i < f.L;
+      // the row's window [lo, i] and its landmark count: sets are ascending with -1 last,
+      // so as unsigned values non-decreasing, and the landmarks the row may use
+      // (0 <= p < min(L, i-w+1)) are a prefix of the set
+      int lo, lcnt;
+      {
+        const int wi = max(S.wv[r], 1);
+        const int lo_raw = i - wi + 1;
+        lo = vrow ? max(lo_raw, 0) : 0x3fffffff;
+        const unsigned lim = vrow ? (unsigned)max(0, min(f.L, lo_raw)) : 0u;
+        int a0 = 0, a1 = p.k_lmk;
+        while (a0 < a1) {
+          const int mid = (a0 + a1) >> 1;
+          if ((unsigned)S.pos[mid] < lim) a0 = mid + 1;
+          else a1 = mid;
+        }
+        lcnt = a0;
+      }
+      mbar_arrive(&B.it_empty[sl_i]);
+      const int NK = f.nwt + f.nlt;
       const float* Bset = p.lmk_bias ? p.lmk_bias + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk : nullptr;
-      float m_acc = -INFINITY, l = 0.0f;  // running max (log2 units, stale by < 2^8) and row sum
+      float m_acc = -INFINITY, l = 0.0f;  // running max (log2 units, stale by at most 2^8) and row sum
       for (int t = 0; t < NK; ++t) {
         if (!mbar_wait(B.s_full, u & 1, p.err, 32)) { ok = false; break; }
         tc_fence_after();
@@ -486,89 +564,144 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int e = 0; e < 32; ++e) x[q * 32 + e] += __shfl_sync(0xffffffffu, bq, e);
           }
         }
-        // row max: the unmasked maximum bounds the masked one and is used unless it would
-        // move the running max by more than the rescale threshold
-        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < BN; c += 8) {
-          m0 = fmax3f(m0, x[c], x[c + 1]);
-          m1 = fmax3f(m1, x[c + 2], x[c + 3]);
-          m2 = fmax3f(m2, x[c + 4], x[c + 5]);
-          m3 = fmax3f(m3, x[c + 6], x[c + 7]);
-        }
-        float m_tile = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * sl;
-        const bool row_all = a <= 0 && b >= BN - 1;
         const float A1 = MASK_C * (0.5f - (float)a), A2 = MASK_C * ((float)b + 0.5f);
-        if (__any_sync(0xffffffffu, !row_all && m_tile > m_acc + RESCALE_THRESHOLD)) {
-          m0 = m1 = m2 = m3 = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < BN; c += 4) {
-            m0 = fmaxf(m0, fmin3f(x[c], fmaf(MASK_C, (float)c, A1), fmaf(-MASK_C, (float)c, A2)));
-            m1 = fmaxf(m1, fmin3f(x[c + 1], fmaf(MASK_C, (float)(c + 1), A1), fmaf(-MASK_C, (float)(c + 1), A2)));
-            m2 = fmaxf(m2, fmin3f(x[c + 2], fmaf(MASK_C, (float)(c + 2), A1), fmaf(-MASK_C, (float)(c + 2), A2)));
-            m3 = fmaxf(m3, fmin3f(x[c + 3], fmaf(MASK_C, (float)(c + 3), A1), fmaf(-MASK_C, (float)(c + 3), A2)));
-          }
-          m_tile = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * sl;
-          if (m_tile < MASKED_MAX) m_tile = -INFINITY;
-        }
-        // rescale only when the row max grows by more than the threshold
-        const bool need = m_tile > m_acc + RESCALE_THRESHOLD;
-        const float m_new = need ? m_tile : m_acc;
-        if (t > 0) {
-          // previous P·V done: P buffer free, O may be rescaled
-          if (!mbar_wait(B.o_full, (u - 1) & 1, p.err, 33)) { ok = false; break; }
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, need)) {
-            const float fac = need ? ex2_approx(m_acc - m_new) : 1.0f;
-#pragma unroll 1
-            for (int cc = 0; cc < HD / 16; ++cc) {
-              uint32_t o[16];
-              DSALT_TMEM_LD16(tO + cc * 16, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
-              DSALT_TMEM_ST16(tO + cc * 16, o);
-            }
-            tmem_wait_st();
-            l *= fac;
-          }
-        }
-        m_acc = m_new;
-        const float mu = (m_acc == -INFINITY) ? 0.0f : m_acc;
-        const uint64_t sl2 = pk2(sl, sl), nmu2 = pk2(-mu, -mu);
         uint64_t s0 = pk2(0.f, 0.f), s1 = s0;
-        // probabilities, row sum, P -> TMEM as 16-bit pairs. Per 32-column chunk the warp
-        // masks only when some lane keeps part of it, and skips the exponentials when no
-        // lane keeps any of it.
+        // Fast path (every tile after the first): exponentials against the running max,
+        // chunk by chunk, P stored to TMEM per chunk once the previous P·V has released the
+        // P buffer. A chunk whose maximum exceeds the running max by more than the rescale
+        // threshold in any lane sends the warp to the slow path, which redoes the tile.
+        // Per 32-column chunk the warp masks only when some lane keeps part of it, and
+        // skips the exponentials when no lane keeps any of it.
+        // chunk classes, warp-uniform: bit c of `none` = no lane keeps chunk c (skipped);
+        // bit c of `all` = every lane keeps all of chunk c (no masking)
+        uint32_t none_l = 0, all_l = 0;
 #pragma unroll
         for (int cc = 0; cc < BN / 32; ++cc) {
-          const int c0 = cc * 32;
-          const bool keep_none = b < c0 || a > c0 + 31;
-          const bool keep_all = a <= c0 && b >= c0 + 31;
-          uint32_t pk[16];
-          if (__all_sync(0xffffffffu, keep_none)) {
+          none_l |= (uint32_t)(b < cc * 32 || a > cc * 32 + 31) << cc;
+          all_l |= (uint32_t)(a <= cc * 32 && b >= cc * 32 + 31) << cc;
+        }
+        const uint32_t none = __reduce_and_sync(0xffffffffu, none_l), all = __reduce_and_sync(0xffffffffu, all_l);
+        bool slow = t == 0, p_free = t == 0;
+        if (!slow) {
+          // exponentials against the running max; the chunk maxima are checked once, after
+          // the tile (a rare overflow redoes the tile on the slow path)
+          const float mu = (m_acc == -INFINITY) ? 0.0f : m_acc;
+          const uint64_t sl2 = pk2(sl, sl), nmu2 = pk2(-mu, -mu);
+          float cm = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) pk[e] = 0u;
-          } else {
+          for (int cc = 0; cc < BN / 32; ++cc) {
+            const int c0 = cc * 32;
+            uint32_t pk[16];
+            if ((none >> cc) & 1) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) pk[e] = 0u;
+            } else {
+              float* xc = x + c0;
+              if (!((all >> cc) & 1)) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e)
+                  xc[e] = fmin3f(xc[e], fmaf(MASK_C, (float)(c0 + e), A1), fmaf(-MASK_C, (float)(c0 + e), A2));
+              }
+              float c0m = fmax3f(xc[0], xc[1], xc[2]), c1m = fmax3f(xc[3], xc[4], xc[5]);
+#pragma unroll
+              for (int e = 6; e < 30; e += 4) {
+                c0m = fmax3f(c0m, xc[e], xc[e + 1]);
+                c1m = fmax3f(c1m, xc[e + 2], xc[e + 3]);
+              }
+              cm = fmax3f(cm, c0m, fmax3f(c1m, xc[30], xc[31]));
+#pragma unroll
+              for (int e = 0; e < 32; e += 4) {
+                const float2 y0 = up2(fma2(pk2(xc[e], xc[e + 1]), sl2, nmu2));
+                const float2 y1 = up2(fma2(pk2(xc[e + 2], xc[e + 3]), sl2, nmu2));
+                const float p0 = ex2_approx(y0.x), p1 = ex2_approx(y0.y);
+                const float p2 = ex2_approx(y1.x), p3 = ex2_approx(y1.y);
+                s0 = add2(s0, pk2(p0, p1));
+                s1 = add2(s1, pk2(p2, p3));
+                pk[e >> 1] = pack_p(bf, p0, p1);
+                pk[(e >> 1) + 1] = pack_p(bf, p2, p3);
+              }
+            }
+            if (!p_free) {
+              // previous P·V done: the P buffer may be overwritten
+              if (!mbar_wait(B.o_full, (u - 1) & 1, p.err, 33)) { ok = false; break; }
+              tc_fence_after();
+              p_free = true;
+            }
+            DSALT_TMEM_ST16(tP + cc * 16, pk);
+          }
+          if (!ok) break;
+          // masked-out columns hold -2^99-scaled values, so cm bounds the kept ones
+          slow = __any_sync(0xffffffffu, cm * sl > m_acc + RESCALE_THRESHOLD && a <= b);
+        }
+        if (slow) {
+          // masked row max; O and the row sum are rescaled when it grows
+          float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+          for (int cc = 0; cc < BN / 32; ++cc) {
+            const int c0 = cc * 32;
+            if ((none >> cc) & 1) continue;
             float* xc = x + c0;
-            if (!__all_sync(0xffffffffu, keep_all)) {
+            if (!((all >> cc) & 1)) {
 #pragma unroll
               for (int e = 0; e < 32; ++e)
                 xc[e] = fmin3f(xc[e], fmaf(MASK_C, (float)(c0 + e), A1), fmaf(-MASK_C, (float)(c0 + e), A2));
             }
 #pragma unroll
             for (int e = 0; e < 32; e += 4) {
-              const float2 y0 = up2(fma2(pk2(xc[e], xc[e + 1]), sl2, nmu2));
-              const float2 y1 = up2(fma2(pk2(xc[e + 2], xc[e + 3]), sl2, nmu2));
-              const float p0 = ex2_approx(y0.x), p1 = ex2_approx(y0.y);
-              const float p2 = ex2_approx(y1.x), p3 = ex2_approx(y1.y);
-              s0 = add2(s0, pk2(p0, p1));
-              s1 = add2(s1, pk2(p2, p3));
-              pk[e >> 1] = bf ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-              pk[(e >> 1) + 1] = bf ? pack_bf16x2(p2, p3) : pack_f16x2(p2, p3);
+              m0 = fmax3f(m0, xc[e], xc[e + 1]);
+              m1 = fmax3f(m1, xc[e + 2], xc[e + 3]);
             }
           }
-          DSALT_TMEM_ST16(tP + cc * 16, pk);
+          float m_tile = fmaxf(m0, m1) * sl;
+          if (m_tile < MASKED_MAX) m_tile = -INFINITY;
+          const bool need = m_tile > m_acc;
+          const float m_new = need ? m_tile : m_acc;
+          if (t > 0) {
+            if (!mbar_wait(B.o_full, (u - 1) & 1, p.err, 33)) { ok = false; break; }
+            tc_fence_after();
+            if (__any_sync(0xffffffffu, need)) {
+              const float fac = need ? ex2_approx(m_acc - m_new) : 1.0f;
+#pragma unroll 1
+              for (int cc = 0; cc < HD / 16; ++cc) {
+                uint32_t o[16];
+                DSALT_TMEM_LD16(tO + cc * 16, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fac);
+                DSALT_TMEM_ST16(tO + cc * 16, o);
+              }
+              tmem_wait_st();
+              l *= fac;
+            }
+          }
+          m_acc = m_new;
+          const float mu = (m_acc == -INFINITY) ? 0.0f : m_acc;
+          const uint64_t sl2 = pk2(sl, sl), nmu2 = pk2(-mu, -mu);
+          s0 = pk2(0.f, 0.f);
+          s1 = s0;
+#pragma unroll
+          for (int cc = 0; cc < BN / 32; ++cc) {
+            const int c0 = cc * 32;
+            uint32_t pk[16];
+            if ((none >> cc) & 1) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) pk[e] = 0u;
+            } else {
+              const float* xc = x + c0;  // masked above where needed
+#pragma unroll
+              for (int e = 0; e < 32; e += 4) {
+                const float2 y0 = up2(fma2(pk2(xc[e], xc[e + 1]), sl2, nmu2));
+                const float2 y1 = up2(fma2(pk2(xc[e + 2], xc[e + 3]), sl2, nmu2));
+                const float p0 = ex2_approx(y0.x), p1 = ex2_approx(y0.y);
+                const float p2 = ex2_approx(y1.x), p3 = ex2_approx(y1.y);
+                s0 = add2(s0, pk2(p0, p1));
+                s1 = add2(s1, pk2(p2, p3));
+                pk[e >> 1] = pack_p(bf, p0, p1);
+                pk[(e >> 1) + 1] = pack_p(bf, p2, p3);
+              }
+            }
+            DSALT_TMEM_ST16(tP + cc * 16, pk);
+          }
         }
         const float2 ss = up2(add2(s0, s1));
         l += ss.x + ss.y;
@@ -642,13 +775,12 @@ static EncodeTiledFn get_encode() {
   return fn;
 }
 
-static int make_map(CUtensorMap* m, const void* base, int dtype, int HD, int heads, int64_t T, int64_t row_stride,
-                    uint32_t box_rows = BM) {
+static int make_map(CUtensorMap* m, const void* base, int dtype, int HD, int heads, int64_t T, int64_t row_stride) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return fail(DSALT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)heads, (cuuint64_t)T};
   const cuuint64_t strides[2] = {(cuuint64_t)HD * 2, (cuuint64_t)row_stride * 2};
-  const cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)BM};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, dtype == DSALT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -662,7 +794,8 @@ static int make_map(CUtensorMap* m, const void* base, int dtype, int HD, int hea
 int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int HD,
                    int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, int32_t* set_base, int32_t* tile_base,
-                   void* out, int out_dtype, float* lse, int* err, cudaStream_t stream) {
+                   int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
+                   cudaStream_t stream) {
   using namespace tc;
   if (HD != 64) return fail(DSALT_ERR_UNSUPPORTED, "attention (tensor cores): head_dim %d not supported (64)", HD);
   if (k_lmk > MAX_LMK) return fail(DSALT_ERR_UNSUPPORTED, "attention: k_lmk %d above %d", k_lmk, MAX_LMK);
@@ -670,15 +803,16 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15 || (q_stride * 2) % 16 ||
       (kv_stride * 2) % 16)
     return fail(DSALT_ERR_INVALID, "attention: q/k/v/out must be 16-byte aligned with 16-byte row strides");
-  CUtensorMap mq, mk, mv, mkr, mvr;
+  CUtensorMap mq, mk, mv;
   int rc;
   if ((rc = make_map(&mq, q, dtype, HD, H, T, q_stride))) return rc;
   if ((rc = make_map(&mk, k, dtype, HD, Hkv, T, kv_stride))) return rc;
   if ((rc = make_map(&mv, v, dtype, HD, Hkv, T, kv_stride))) return rc;
-  if ((rc = make_map(&mkr, k, dtype, HD, Hkv, T, kv_stride, 1))) return rc;  // one-row boxes: landmark gather
-  if ((rc = make_map(&mvr, v, dtype, HD, Hkv, T, kv_stride, 1))) return rc;
   if ((rc = launch_chunk_table(cu, n_seqs, BM, tile_base, stream))) return rc;
   if (lmk_block > 0 && (rc = launch_chunk_table(cu, n_seqs, lmk_block, set_base, stream))) return rc;
+  tile_plan_kernel<<<(unsigned)((max_tiles + 7) / 8), 256, 0, stream>>>(cu, n_seqs, tile_base, set_base, lmk_block, w,
+                                                                       plan);
+  if ((rc = check_cuda(cudaGetLastError(), "tile plan launch"))) return rc;
   Params p{};
   p.k = k;
   p.v = v;
@@ -694,6 +828,7 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   p.n_seqs = n_seqs;
   p.set_base = set_base;
   p.tile_base = tile_base;
+  p.plan = plan;
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
   p.inv_scale = (float)sqrt((double)HD);
   const uint32_t ab = dtype == DSALT_BF16 ? 1u : 0u;
@@ -711,11 +846,11 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   const int grid = (int)(want < nsm ? want : nsm);
   if (grid <= 0) return DSALT_OK;
   const size_t smem = Smem<64>::BYTES + 1024;
-  if ((rc = check_cuda(cudaFuncSetAttribute(attn_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)smem),
+  auto kern = dtype == DSALT_BF16 ? attn_fwd_tc_kernel<64, true> : attn_fwd_tc_kernel<64, false>;
+  if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "attention smem attr")))
     return rc;
-  attn_fwd_tc_kernel<64><<<grid, NTHREADS, smem, stream>>>(mq, mk, mv, mkr, mvr, p);
+  kern<<<grid, NTHREADS, smem, stream>>>(mq, mk, mv, p);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 

@@ -28,7 +28,8 @@ int launch_attn_f32(const float* q, const float* k, const float* v, int64_t T, i
 int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int HD,
                    int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, int32_t* set_base, int32_t* tile_base,
-                   void* out, int out_dtype, float* lse, int* err, cudaStream_t stream);
+                   int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
+                   cudaStream_t stream);
 int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream);
 
 // ---------------------------------------------------------------- errors
@@ -69,11 +70,14 @@ int* device_status_ptr() {
   return ptrs[dev];
 }
 
-// Scratch of dsalt_attention_fwd_noalloc: the query-tile and landmark-set tables for up
-// to DSALT_NOALLOC_MAX_SEQS sequences, laid out as dsalt_attention_fwd carves its
-// workspace (two 256-byte aligned tables of n_seqs + 1 int32).
+// Scratch of dsalt_attention_fwd_noalloc, laid out as dsalt_attention_fwd carves its
+// workspace: the landmark-set and query-tile tables (n_seqs + 1 int32 each) and the
+// per-tile plan (32 bytes per 128-query tile), sized for DSALT_NOALLOC_MAX_SEQS sequences
+// and DSALT_NOALLOC_MAX_TOKENS tokens.
 constexpr size_t NOALLOC_TABLE_BYTES = ((DSALT_NOALLOC_MAX_SEQS + 1) * sizeof(int32_t) + 255) & ~(size_t)255;
-static __device__ __align__(256) int32_t g_noalloc_scratch[2 * NOALLOC_TABLE_BYTES / sizeof(int32_t)];
+constexpr size_t NOALLOC_PLAN_BYTES = (size_t)(DSALT_NOALLOC_MAX_TOKENS / 128 + DSALT_NOALLOC_MAX_SEQS) * 32;
+static __device__ __align__(256) int32_t
+    g_noalloc_scratch[(2 * NOALLOC_TABLE_BYTES + NOALLOC_PLAN_BYTES) / sizeof(int32_t)];
 
 static void* noalloc_scratch_ptr() {
   static std::mutex mu;
@@ -138,13 +142,15 @@ int dsalt_select_landmarks(int mode, const float* xnorm, const float* vnorm, con
                        lmk_out, zx_out, zv_out, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// landmark-set table | query-tile table | per-tile plan (tensor-core path)
+static inline int64_t attention_max_tiles(int64_t T, int n_seqs) { return T / 128 + n_seqs; }
+
 size_t dsalt_attention_workspace_bytes(int64_t T, int n_seqs, int n_heads, int k_lmk, int lmk_block) {
-  (void)T;
   (void)n_heads;
   (void)k_lmk;
   (void)lmk_block;
-  if (n_seqs < 1) return 0;
-  return 2 * a256(sizeof(int32_t) * (size_t)(n_seqs + 1));
+  if (n_seqs < 1 || T < 0) return 0;
+  return 2 * a256(sizeof(int32_t) * (size_t)(n_seqs + 1)) + a256(32 * (size_t)attention_max_tiles(T, n_seqs));
 }
 
 int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
@@ -167,8 +173,9 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
   const size_t need = dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k_lmk, lmk_block);
   if (workspace_bytes < need) return fail(DSALT_ERR_WORKSPACE, "attention: workspace %zu < %zu", workspace_bytes, need);
   int32_t* set_base = reinterpret_cast<int32_t*>(workspace);
-  int32_t* tile_base = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) +
-                                                  a256(sizeof(int32_t) * (size_t)(n_seqs + 1)));
+  const size_t table_bytes = a256(sizeof(int32_t) * (size_t)(n_seqs + 1));
+  int32_t* tile_base = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + table_bytes);
+  int4* plan = reinterpret_cast<int4*>(reinterpret_cast<char*>(workspace) + 2 * table_bytes);
   if (dtype == DSALT_F32) {
     int rc = DSALT_OK;
     if (lmk_block > 0 && (rc = launch_chunk_table(cu_seqlens, n_seqs, lmk_block, set_base, s))) return rc;
@@ -178,8 +185,8 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
                            (float)(1.0 / sqrt((double)head_dim)), out, out_dtype, lse, s);
   }
   return launch_attn_tc(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
-                        lmk_block, cu_seqlens, n_seqs, set_base, tile_base, out, out_dtype, lse, device_status_ptr(),
-                        s);
+                        lmk_block, cu_seqlens, n_seqs, set_base, tile_base, plan, attention_max_tiles(T, n_seqs), out,
+                        out_dtype, lse, device_status_ptr(), s);
 }
 
 // Callers without a device allocator (bindings that hold only the caller's pointers,
@@ -190,11 +197,11 @@ int dsalt_attention_fwd_noalloc(const void* q, const void* k, const void* v, int
                                 const int32_t* lmk, const float* lmk_bias, int k_lmk, int lmk_block,
                                 const int32_t* cu_seqlens, int n_seqs, int max_seqlen, void* out, int out_dtype,
                                 float* lse, void* stream) {
-  if (n_seqs > DSALT_NOALLOC_MAX_SEQS)
+  if (n_seqs > DSALT_NOALLOC_MAX_SEQS || T > DSALT_NOALLOC_MAX_TOKENS)
     return fail(DSALT_ERR_UNSUPPORTED,
-                "attention (no-alloc): n_seqs %d above the static scratch limit %d; use dsalt_attention_fwd with a "
-                "workspace",
-                n_seqs, DSALT_NOALLOC_MAX_SEQS);
+                "attention (no-alloc): n_seqs %d / T %lld above the static scratch limit (%d sequences, %d tokens); "
+                "use dsalt_attention_fwd with a workspace",
+                n_seqs, (long long)T, DSALT_NOALLOC_MAX_SEQS, DSALT_NOALLOC_MAX_TOKENS);
   const size_t need = dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k_lmk, lmk_block);
   if (need > sizeof(g_noalloc_scratch))
     return fail(DSALT_ERR_UNSUPPORTED, "attention (no-alloc): scratch %zu above %zu", need,
@@ -227,7 +234,6 @@ int dsalt_core_forward(int mode, const void* x, int x_dtype, int d_model, int64_
                        int head_dim, int64_t q_stride, int64_t kv_stride, int k_lmk, int block,
                        const int32_t* cu_seqlens, int n_seqs, int64_t T, int max_seqlen, void* out, int out_dtype,
                        int32_t* w_out, int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream) {
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (mode != DSALT_SELECT_GLOBAL && mode != DSALT_SELECT_BLOCK_CAUSAL) return fail(DSALT_ERR_INVALID, "core: mode");
   if (T < 0 || n_seqs < 1) return fail(DSALT_ERR_INVALID, "core: bad sizes");
   if (T == 0) return DSALT_OK;
@@ -258,7 +264,6 @@ int dsalt_core_forward(int mode, const void* x, int x_dtype, int d_model, int64_
   return dsalt_attention_fwd(q, k, v, qkv_dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, nullptr,
                              k_lmk, mode == DSALT_SELECT_GLOBAL ? 0 : block, cu_seqlens, n_seqs, max_seqlen, out,
                              out_dtype, nullptr, aws, aws_bytes, stream);
-  (void)s;
 }
 
 }  // extern "C"

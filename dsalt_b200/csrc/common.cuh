@@ -187,6 +187,16 @@ __device__ __forceinline__ void cp_async_16(uint32_t smem_addr, const void* gmem
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
                : "memory");
 }
+// 4-byte cp.async (zero-filled when src_bytes == 0)
+__device__ __forceinline__ void cp_async_4(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+// the mbarrier's pending count is raised by one now and lowered when this thread's prior
+// cp.async operations have completed
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

@@ -122,10 +122,11 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
  * caller's q/k/v/out pointers and no device allocator of its own (a cgo, JNI or ctypes
  * binding with no framework behind it), or a serving loop whose memory pool is fully
  * reserved for its caches and may not grow between requests. The scratch that
- * dsalt_attention_fwd takes from `workspace` (two sequence tables, 2 x (n_seqs+1) int32)
- * comes here from a static device array of this library, one per device:
- *   - at most DSALT_NOALLOC_MAX_SEQS sequences; larger n_seqs fails with
- *     DSALT_ERR_UNSUPPORTED before any work is queued;
+ * dsalt_attention_fwd takes from `workspace` (two sequence tables of n_seqs+1 int32 and a
+ * 32-byte plan per 128-query tile) comes here from a static device array of this library
+ * (417 KB), one per device:
+ *   - at most DSALT_NOALLOC_MAX_SEQS sequences and DSALT_NOALLOC_MAX_TOKENS tokens;
+ *     larger requests fail with DSALT_ERR_UNSUPPORTED before any work is queued;
  *   - nothing in it needs to start at zero: each call rewrites the tables it reads;
  *   - every call on a device shares it, so calls that may overlap on one device (other
  *     streams, other host threads) race on it; the caller serialises them;
@@ -135,6 +136,7 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
  * error codes are otherwise those of dsalt_attention_fwd (the same kernels run).
  */
 #define DSALT_NOALLOC_MAX_SEQS 4096
+#define DSALT_NOALLOC_MAX_TOKENS 1048576
 int dsalt_attention_fwd_noalloc(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads,
                                 int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, const int32_t* w,
                                 const int32_t* lmk, const float* lmk_bias, int k_lmk, int lmk_block,

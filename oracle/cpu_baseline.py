@@ -2,12 +2,18 @@
 
 TEST/BENCH INFRASTRUCTURE ONLY (imported by ``bench.py``'s CPU-baseline legs).
 
-Follows ``results/causal_landmark_check.py``: prefix statistics in float64 cumsums
+Follows ``results/causal_landmark_check.py``: token signals (``_token_signals``
+``:68-79``: ``‖x‖``, value norms) and window widths
+(``dsalt/modules/dsalt_attention.py:270-284``), prefix statistics in float64 cumsums
 (``_prefix_stats`` ``:82-85``, ``_std_at`` ``:88-92``), per-block top-k over the prefix
 (``_select`` ``:95-113``) and the fp32 masked attention of ``_block_attention``
 (``:119-147``), per 512-query block (``:183-186``). The masked-SDPA fallback of the
 reference needs ``[T, T]`` masks and is infeasible at L=131072, so this is the CPU path
 that is timed for that configuration.
+
+The sequence is processed as a stream of blocks: a step over blocks ``[b0, b1)`` computes
+the signals and widths of those blocks' tokens, extends the prefix sums, then selects
+and attends each block, so every step is charged exactly the work of its own tokens.
 """
 from __future__ import annotations
 
@@ -18,21 +24,55 @@ import torch
 
 
 class BlockCausalCPU:
-    def __init__(self, q, k, v, w, xn, vn, alpha, k_lmk, block=512):
+    def __init__(self, x, gate_w, gate_b, n_min, n_max, q, k, v, alpha, k_lmk, block=512):
+        self.x = x                      # [T, d_model] (bf16 as given)
+        self.gw = gate_w.float()
+        self.gb = float(gate_b.float().reshape(-1)[0])
+        self.n_min, self.n_max = n_min, n_max
         self.q = q.float()
         self.k = k.float()
         self.v = v.float()
-        self.w = w.long()
-        self.xn = xn.double()
-        self.vn = vn.double()
         self.alpha = alpha.float()
         self.k_lmk = k_lmk
         self.B = block
         self.T, self.H, self.D = self.q.shape
-        self.sx = (torch.cumsum(self.xn, 0), torch.cumsum(self.xn * self.xn, 0))
-        self.sv = (torch.cumsum(self.vn, 0), torch.cumsum(self.vn * self.vn, 0))
-        self.covered = torch.arange(self.T) < self.w
+        self.n_kv = self.k.shape[1]
         self.scale = 1.0 / math.sqrt(self.D)
+        self.reset()
+
+    def reset(self):
+        T = self.T
+        self.w = torch.empty(T, dtype=torch.long)
+        self.xn = torch.empty(T, dtype=torch.float64)
+        self.vn = torch.empty(T, self.n_kv, dtype=torch.float64)
+        self.sx = (torch.empty(T, dtype=torch.float64), torch.empty(T, dtype=torch.float64))
+        self.sv = (torch.empty(T, self.n_kv, dtype=torch.float64), torch.empty(T, self.n_kv, dtype=torch.float64))
+        self.covered = torch.empty(T, dtype=torch.bool)
+        self.done = 0  # tokens whose signals and prefix sums exist
+
+    def signals(self, t1):
+        """Signals, widths and prefix sums of tokens [done, t1)."""
+        t0 = self.done
+        if t1 <= t0:
+            return
+        xs = self.x[t0:t1].float()
+        logit = xs @ self.gw + self.gb
+        w = torch.floor(self.n_min + torch.sigmoid(logit) * (self.n_max - self.n_min)).clamp(min=1).long()
+        self.w[t0:t1] = w
+        self.covered[t0:t1] = torch.arange(t0, t1) < w
+        xn = xs.norm(dim=-1).double()
+        vn = self.v[t0:t1].norm(dim=-1).double()
+        self.xn[t0:t1] = xn
+        self.vn[t0:t1] = vn
+        for (S1, S2), val in ((self.sx, xn), (self.sv, vn)):
+            c1 = torch.cumsum(val, 0)
+            c2 = torch.cumsum(val * val, 0)
+            if t0 > 0:
+                c1 += S1[t0 - 1]
+                c2 += S2[t0 - 1]
+            S1[t0:t1] = c1
+            S2[t0:t1] = c2
+        self.done = t1
 
     @staticmethod
     def _std_at(S1, S2, n):
@@ -87,12 +127,15 @@ class BlockCausalCPU:
     def run_block(self, b):
         b0 = b * self.B
         b1 = min(self.T, b0 + self.B)
+        self.signals(b1)
         return self.attend(self.select(b0), b0, b1)
 
-    def time_sample(self, blocks):
+    def time_blocks(self, b0, b1):
+        """Stream blocks [b0, b1) (restarting the stream when b0 == 0); (tokens, seconds)."""
+        if b0 == 0:
+            self.reset()
         t0 = time.perf_counter()
-        for b in blocks:
+        for b in range(b0, b1):
             self.run_block(b)
         dt = time.perf_counter() - t0
-        tokens = sum(min(self.T, (b + 1) * self.B) - b * self.B for b in blocks)
-        return tokens, dt
+        return min(self.T, b1 * self.B) - b0 * self.B, dt

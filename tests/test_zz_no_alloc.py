@@ -70,13 +70,16 @@ def _no_alloc(p):
     return out, lse
 
 
-def test_no_alloc_rejects_more_sequences_than_its_scratch_holds():
+def test_no_alloc_rejects_more_than_its_scratch_holds():
     # checked before any CUDA call: runs without a GPU
     lib = L.load()
     rc = lib.dsalt_attention_fwd_noalloc(None, None, None, L.BF16, 8, 1, 1, 64, 64, 64, None, None, None, 0, 0,
                                          None, L.NOALLOC_MAX_SEQS + 1, 8, None, L.BF16, None, None)
     assert rc == L.ERR_UNSUPPORTED
     assert b"static scratch limit" in lib.dsalt_last_error()
+    rc = lib.dsalt_attention_fwd_noalloc(None, None, None, L.BF16, L.NOALLOC_MAX_TOKENS + 1, 1, 1, 64, 64, 64, None,
+                                         None, None, 0, 0, None, 1, 8, None, L.BF16, None, None)
+    assert rc == L.ERR_UNSUPPORTED
 
 
 @pytest.mark.gpu
