@@ -184,12 +184,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // cp.async (16 bytes, zero-filled when src_bytes == 0) and its mbarrier tracking
 __device__ __forceinline__ void cp_async_16(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(__cvta_generic_to_global(gmem)),
+               "r"(src_bytes)
                : "memory");
 }
 // 4-byte cp.async (zero-filled when src_bytes == 0)
 __device__ __forceinline__ void cp_async_4(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr), "l"(gmem), "r"(src_bytes)
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr), "l"(__cvta_generic_to_global(gmem)),
+               "r"(src_bytes)
                : "memory");
 }
 // the mbarrier's pending count is raised by one now and lowered when this thread's prior

@@ -380,6 +380,22 @@ __global__ void __launch_bounds__(SEL_THREADS) global_phase2_kernel(const uint64
   }
 }
 
+// fp32 of the correctly rounded float64 quotient (v - mean) / sd, as the reference's
+// float64 z-score cast to float32 (causal_landmark_check.py:104-105). The quotient is taken
+// as (v - mean) * (1/sd), within 2 float64 ulps of the correctly rounded one; unless that
+// lies within 4 ulps of a float32 rounding boundary (the 29 dropped mantissa bits close to
+// their midpoint), both round to the same float32. Otherwise, and for tiny quotients, the
+// exact division decides.
+__device__ __forceinline__ float z_score(float v, double mean, double sd, double rinv) {
+  const double d = __dsub_rn((double)v, mean);
+  const double q = __dmul_rn(d, rinv);
+  const long long bits = __double_as_longlong(q);
+  const long long dropped = bits & ((1ll << 29) - 1);
+  const long long dist = dropped - (1ll << 28);
+  if ((dist > 4 || dist < -4) && fabs(q) > 1e-30) return __double2float_rn(q);
+  return __double2float_rn(__ddiv_rn(d, sd));
+}
+
 // ---------------------------------------------------------------------------
 // block-causal: prefix statistics per block and dominance-grid thresholds
 // stats[set][sig] = (mean, sd) float64 of positions [0, b·C) (_std_at,
@@ -518,21 +534,32 @@ __global__ void dominance_scan_kernel(int32_t* __restrict__ G, const int32_t* __
   const int cell = blockIdx.y * blockDim.x + threadIdx.x;
   if (cell >= NCELL) return;
   int run = 0;
-  for (int c = base[s]; c < base[s + 1]; ++c) {
-    int32_t* p = G + ((int64_t)c * n_kv + g) * NCELL + cell;
-    const int v = *p;
-    *p = run;
-    run += v;
+  const int c_end = base[s + 1];
+  const int64_t stride = (int64_t)n_kv * NCELL;
+  // batches of 16 chunks: all loads of a batch are in flight before its stores
+  for (int c0 = base[s]; c0 < c_end; c0 += 16) {
+    int32_t* p = G + ((int64_t)c0 * n_kv + g) * NCELL + cell;
+    int v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = c0 + j < c_end ? p[j * stride] : 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (c0 + j < c_end) p[j * stride] = run;
+      run += v[j];
+    }
   }
 }
 
 // survivors: uncovered tokens dominated (strictly, in both signals) by fewer than k
-// uncovered tokens of earlier chunks; written in position order per (chunk, group)
+// uncovered tokens of earlier chunks; written in position order per (chunk, group) as
+// records {position, ‖x‖, value norm of the group, dominance cell}, the cell being the
+// grid index whose prefix count bounds the token's dominators from below (-1: none can
+// dominate it)
 __global__ void survivor_kernel(const float* __restrict__ xn, const float* __restrict__ vn,
                                 const int32_t* __restrict__ w, int n_kv, const int32_t* __restrict__ cu, int n_seqs,
                                 const int32_t* __restrict__ base, int C, const float* __restrict__ edges,
                                 const int32_t* __restrict__ D, int k, int32_t* __restrict__ surv_cnt,
-                                int32_t* __restrict__ surv_pos) {
+                                int4* __restrict__ surv_rec) {
   __shared__ float ex[NBIN - 1], ev[NBIN - 1];
   __shared__ int32_t wsum[32];
   const int c = blockIdx.x, g = blockIdx.y, nsig = 1 + n_kv;
@@ -548,18 +575,22 @@ __global__ void survivor_kernel(const float* __restrict__ xn, const float* __res
   const int p0 = (c - base[s]) * C;
   const int p1 = min(cu[s + 1] - start, p0 + C);
   const int32_t* Dc = D + ((int64_t)c * n_kv + g) * NCELL;
-  int32_t* outp = surv_pos + ((int64_t)c * n_kv + g) * C;
+  int4* outp = surv_rec + ((int64_t)c * n_kv + g) * C;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   int carry = 0;
   for (int q0 = p0; q0 < p1; q0 += blockDim.x) {
     const int p = q0 + threadIdx.x;
     int keep = 0;
+    int4 rec;
     if (p < p1) {
       const int64_t t = start + p;
       if (p >= w[t]) {
-        const int a = bin_of(vn[t * n_kv + g], ev), b = bin_of(xn[t], ex);
-        const int dom = (a == NBIN - 1 || b == NBIN - 1) ? 0 : Dc[(a + 1) * NBIN + (b + 1)];
+        const float xv = xn[t], vv = vn[t * n_kv + g];
+        const int a = bin_of(vv, ev), b = bin_of(xv, ex);
+        const int cell = (a == NBIN - 1 || b == NBIN - 1) ? -1 : (a + 1) * NBIN + (b + 1);
+        const int dom = cell < 0 ? 0 : Dc[cell];
         keep = dom < k;
+        rec = make_int4(p, __float_as_int(xv), __float_as_int(vv), cell);
       }
     }
     const unsigned ball = __ballot_sync(0xffffffffu, keep);
@@ -568,7 +599,7 @@ __global__ void survivor_kernel(const float* __restrict__ xn, const float* __res
     int before = carry;
     for (int j = 0; j < wid; ++j) before += wsum[j];
     before += __popc(ball & ((1u << lane) - 1));
-    if (keep) outp[before] = p;
+    if (keep) outp[before] = rec;
     int tot = 0;
     for (int j = 0; j < nw; ++j) tot += wsum[j];
     carry += tot;
@@ -581,14 +612,16 @@ __global__ void survivor_kernel(const float* __restrict__ xn, const float* __res
 __global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w,
     const float* __restrict__ alpha, const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base,
-    int C, int n_heads, int n_kv, int k, const double2* __restrict__ stats, const int32_t* __restrict__ surv_cnt,
-    const int32_t* __restrict__ surv_pos, int32_t* __restrict__ lmk_out) {
+    int C, int n_heads, int n_kv, int k, const double2* __restrict__ stats, const int32_t* __restrict__ D,
+    const int32_t* __restrict__ surv_cnt, const int4* __restrict__ surv_rec, int32_t* __restrict__ lmk_out) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
   __shared__ TopkSmem sm;
   __shared__ int32_t sel[MAX_K];
   __shared__ int32_t offs[1025];
   __shared__ int32_t wsum[32];
+  __shared__ int32_t dsm[NCELL];
+  __shared__ int32_t ncand;
   const int c = blockIdx.x, h = blockIdx.y;
   const int total = base[n_seqs];
   if (c >= total) return;
@@ -606,11 +639,12 @@ __global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
   const double2 stv = stats[(int64_t)c * nsig + 1 + g];
   const float a = alpha[h];
   const bool pruned = (a >= 0.0f && a <= 1.0f) && b <= 1024;
+  const double rx = __drcp_rn(stx.y), rv = __drcp_rn(stv.y);
   auto score_key = [&](int p) -> uint64_t {
     const int64_t t = start + p;
     if (p >= n || p < w[t]) return 0ull;
-    const float zx = __double2float_rn(__ddiv_rn(__dsub_rn((double)xn[t], stx.x), stx.y));
-    const float zv = __double2float_rn(__ddiv_rn(__dsub_rn((double)vn[t * n_kv + g], stv.x), stv.y));
+    const float zx = z_score(xn[t], stx.x, stx.y, rx);
+    const float zv = z_score(vn[t * n_kv + g], stv.x, stv.y, rv);
     const float sc = __fadd_rn(__fmul_rn(a, zv), __fmul_rn(__fsub_rn(1.0f, a), zx));
     return make_key(sc, p);
   };
@@ -648,24 +682,66 @@ __global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
     carry += tot;
     __syncthreads();
   }
-  if (threadIdx.x == 0) offs[b] = carry;
+  if (threadIdx.x == 0) {
+    offs[b] = carry;
+    ncand = 0;
+  }
+  // dominators of every grid cell among all uncovered tokens of the block's prefix
+  const int32_t* Dc = D + ((int64_t)c * n_kv + g) * NCELL;
+  for (int i = threadIdx.x; i < NCELL; i += blockDim.x) dsm[i] = Dc[i];
   __syncthreads();
-  const int N = offs[b];
-  auto cand_pos = [&](int i) -> int {
-    int lo = 0, hi = b;  // offs[lo] <= i < offs[lo+1]
+  // Candidates: survivors of the earlier chunks that are still dominated by fewer than k
+  // tokens of the whole prefix (a token with >= k dominators is outranked by them for any
+  // alpha in [0, 1]), compacted into shared memory.
+  const float a1 = __fsub_rn(1.0f, a);
+  auto rec_key = [&](int4 r) -> uint64_t {
+    const float zx = z_score(__int_as_float(r.y), stx.x, stx.y, rx);
+    const float zv = z_score(__int_as_float(r.z), stv.x, stv.y, rv);
+    const float sc = __fadd_rn(__fmul_rn(a, zv), __fmul_rn(a1, zx));
+    return make_key(sc, r.x);
+  };
+  // survivor i of the prefix lies in chunk j with offs[j] <= i < offs[j+1]
+  auto rec_of = [&](int i) -> const int4* {
+    int lo = 0, hi = b;
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
       if (offs[mid] <= i) lo = mid;
       else hi = mid;
     }
-    return surv_pos[((int64_t)(c0 + lo) * n_kv + g) * C + (i - offs[lo])];
+    return surv_rec + ((int64_t)(c0 + lo) * n_kv + g) * C + (i - offs[lo]);
   };
+  const int NS = offs[b];
+  constexpr int U = 4;  // records per thread in flight
+  for (int i0 = threadIdx.x; i0 - (int)threadIdx.x < NS; i0 += U * blockDim.x) {
+    int4 r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * blockDim.x;
+      r[u] = i < NS ? *rec_of(i) : make_int4(0, 0, 0, 0x7fffffff);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool live = r[u].w != 0x7fffffff && (r[u].w < 0 || dsm[r[u].w] < k);
+      const uint64_t key = live ? rec_key(r[u]) : 0ull;
+      const unsigned ball = __ballot_sync(0xffffffffu, key != 0);
+      int slot0 = 0;
+      if (lane == 0 && ball) slot0 = atomicAdd(&ncand, __popc(ball));
+      slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+      const int slot = slot0 + __popc(ball & ((1u << lane) - 1));
+      if (key != 0 && slot < KEY_CAP) keys[slot] = key;
+    }
+  }
+  __syncthreads();
+  const int N = ncand;
   if (N <= KEY_CAP) {
-    for (int i = threadIdx.x; i < N; i += blockDim.x) keys[i] = score_key(cand_pos(i));
-    __syncthreads();
     block_topk_positions([&](int i) { return keys[i]; }, N, k, sm, sel, out);
   } else {
-    block_topk_positions([&](int i) { return score_key(cand_pos(i)); }, N, k, sm, sel, out);
+    // more candidates than the cache holds: evaluate them from the survivor lists
+    auto cand_key = [&](int i) -> uint64_t {
+      const int4 r = *rec_of(i);
+      return (r.w < 0 || dsm[r.w] < k) ? rec_key(r) : 0ull;
+    };
+    block_topk_positions(cand_key, NS, k, sm, sel, out);
   }
 }
 
@@ -707,7 +783,7 @@ static SelectLayout select_layout(int mode, int64_t T, int n_seqs, int n_heads, 
     L.cnt_off = off;
     off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv);
     L.pos_off = off;
-    off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv * C);
+    off = align256(off + sizeof(int4) * (size_t)L.max_chunks * n_kv * C);
   }
   L.total = off;
   return L;
@@ -784,16 +860,16 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
     float* edges = reinterpret_cast<float*>(ws + L.edges_off);
     int32_t* G = reinterpret_cast<int32_t*>(ws + L.G_off);
     int32_t* cnt = reinterpret_cast<int32_t*>(ws + L.cnt_off);
-    int32_t* pos = reinterpret_cast<int32_t*>(ws + L.pos_off);
+    int4* recs = reinterpret_cast<int4*>(ws + L.pos_off);
     block_stats_kernel<<<dim3(n_seqs, nsig), 256, 0, stream>>>(part, cu, n_seqs, cbase, nsig, C, stats, edges);
     dominance_hist_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
                                                                         edges, G);
     dominance_scan_kernel<<<dim3(n_seqs * n_kv, NCELL / 256), 256, 0, stream>>>(G, cbase, n_kv);
     survivor_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges,
-                                                                  G, k, cnt, pos);
+                                                                  G, k, cnt, recs);
     const size_t sm3 = sizeof(uint64_t) * KEY_CAP;
     block_select_kernel<<<dim3(L.max_chunks, n_heads), SEL_THREADS, sm3, stream>>>(
-        xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, cnt, pos, lmk_out);
+        xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, G, cnt, recs, lmk_out);
   }
   return check_cuda(cudaGetLastError(), "select launch");
 }

@@ -11,7 +11,8 @@
 //    then every op of `n_min + σ·(n_max−n_min)` rounds to the gate dtype, floor, >= 1;
 //  * norms: sum of squares in float64 rounded once to fp32, IEEE fp32 sqrt, optionally
 //    rounded to the input dtype.
-// One warp per token; 16-byte vector loads; HBM-bound (reads x and v once).
+// One warp per token; 16-byte vector loads; HBM-bound (reads x and v once). The wide
+// variant issues all of a token's loads up front (enough bytes in flight for HBM rate).
 #include "common.cuh"
 
 namespace dsalt {
@@ -20,7 +21,9 @@ template <int DT> struct Vec;
 template <> struct Vec<DSALT_BF16> {
   static constexpr int N = 8;
   static __device__ __forceinline__ void load(const void* p, float* out) {
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    unpack(__ldg(reinterpret_cast<const uint4*>(p)), out);
+  }
+  static __device__ __forceinline__ void unpack(uint4 u, float* out) {
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -33,7 +36,9 @@ template <> struct Vec<DSALT_BF16> {
 template <> struct Vec<DSALT_F16> {
   static constexpr int N = 8;
   static __device__ __forceinline__ void load(const void* p, float* out) {
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    unpack(__ldg(reinterpret_cast<const uint4*>(p)), out);
+  }
+  static __device__ __forceinline__ void unpack(uint4 u, float* out) {
     const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -154,6 +159,120 @@ __global__ void __launch_bounds__(256) token_signals_kernel(
   }
 }
 
+// Four 16-byte read-only loads issued as one block, so that they are all in flight before
+// the first result is used
+__device__ __forceinline__ void ldg16x4(const uint4* q0, const uint4* q1, const uint4* q2, const uint4* q3,
+                                        uint4* r) {
+  const size_t p0 = __cvta_generic_to_global(q0), p1 = __cvta_generic_to_global(q1);
+  const size_t p2 = __cvta_generic_to_global(q2), p3 = __cvta_generic_to_global(q3);
+  asm volatile(
+      "ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%16];\n\t"
+      "ld.global.nc.v4.u32 {%4, %5, %6, %7}, [%17];\n\t"
+      "ld.global.nc.v4.u32 {%8, %9, %10, %11}, [%18];\n\t"
+      "ld.global.nc.v4.u32 {%12, %13, %14, %15}, [%19];"
+      : "=r"(r[0].x), "=r"(r[0].y), "=r"(r[0].z), "=r"(r[0].w), "=r"(r[1].x), "=r"(r[1].y), "=r"(r[1].z),
+        "=r"(r[1].w), "=r"(r[2].x), "=r"(r[2].y), "=r"(r[2].z), "=r"(r[2].w), "=r"(r[3].x), "=r"(r[3].y),
+        "=r"(r[3].z), "=r"(r[3].w)
+      : "l"(p0), "l"(p1), "l"(p2), "l"(p3));
+}
+
+// Same arithmetic (and accumulation order) as token_signals_kernel, for 16-bit x and v
+// whose rows split into at most XCM (x) / VCM (v) 16-byte chunks per lane: every load of
+// a token is issued before any is used, so a warp keeps its whole token (up to 8 KB) in
+// flight; the gate weights sit in shared memory as fp64 (fp32->fp64 conversions run at a
+// quarter of the fp64 FMA rate, so each element is converted once).
+template <int XDT, int VDT, int XCM, int VCM>
+__global__ void __launch_bounds__(256) token_signals_wide_kernel(
+    const void* __restrict__ x, int64_t T, int d_model, int64_t x_stride, const void* __restrict__ gate_w,
+    const void* __restrict__ gate_b, int gate_dt, int n_min, int n_max, const void* __restrict__ v, int64_t v_stride,
+    int n_kv, int head_dim, int norm_mode, int32_t* __restrict__ w_out, float* __restrict__ xnorm_out,
+    float* __restrict__ vnorm_out, float* __restrict__ logit_out) {
+  constexpr int XN = Vec<XDT>::N;
+  constexpr int VN = Vec<VDT>::N;
+  extern __shared__ double gws[];
+  for (int i = threadIdx.x; i < d_model; i += blockDim.x) gws[i] = (double)load_elem(gate_w, i, gate_dt);
+  __syncthreads();
+  // x is converted to the gate dtype before the product; for a gate in fp32 or in x's own
+  // dtype that conversion is the identity, and one fp32->fp64 conversion serves both sums
+  const bool xg_is_x = gate_dt == DSALT_F32 || gate_dt == XDT;
+  const int lane = threadIdx.x & 31;
+  const int warps_per_block = blockDim.x >> 5;
+  const int64_t warp0 = (int64_t)blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * warps_per_block;
+  const int xc = d_model / XN / 32;                 // x chunks per lane (<= XCM)
+  const int vcpg = head_dim / VN;                    // v chunks per kv group (<= 32, power of two)
+  const int vc = n_kv * vcpg / 32;                   // v chunks per lane (<= VCM)
+  const double bias = (double)load_elem(gate_b, 0, gate_dt);
+  for (int64_t t = warp0; t < T; t += nwarps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(elem_ptr<XDT>(x, t * x_stride));
+    const uint4* vr = reinterpret_cast<const uint4*>(elem_ptr<VDT>(v, t * v_stride));
+    // chunks past the row's end re-read chunk 0 (an L1 hit) and are not used
+    uint4 xq[XCM], vq[VCM];
+#pragma unroll
+    for (int j = 0; j < XCM; j += 4)
+      ldg16x4(xr + lane + 32 * (j < xc ? j : 0), xr + lane + 32 * (j + 1 < xc ? j + 1 : 0),
+              xr + lane + 32 * (j + 2 < xc ? j + 2 : 0), xr + lane + 32 * (j + 3 < xc ? j + 3 : 0), xq + j);
+#pragma unroll
+    for (int j = 0; j < VCM; j += 4)
+      ldg16x4(vr + lane + 32 * (j < vc ? j : 0), vr + lane + 32 * (j + 1 < vc ? j + 1 : 0),
+              vr + lane + 32 * (j + 2 < vc ? j + 2 : 0), vr + lane + 32 * (j + 3 < vc ? j + 3 : 0), vq + j);
+    double dot = 0.0, sq = 0.0;
+#pragma unroll
+    for (int j = 0; j < XCM; ++j) {
+      if (j < xc) {
+        float xv[XN];
+        Vec<XDT>::unpack(xq[j], xv);
+        const int c = lane + 32 * j;
+        if (xg_is_x) {
+#pragma unroll
+          for (int i = 0; i < XN; ++i) {
+            const double xd = (double)xv[i];
+            dot = __fma_rn(xd, gws[c * XN + i], dot);
+            sq = __fma_rn(xd, xd, sq);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < XN; ++i) {
+            const double xd = (double)xv[i];
+            dot = __fma_rn((double)round_to(xv[i], gate_dt), gws[c * XN + i], dot);
+            sq = __fma_rn(xd, xd, sq);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    }
+    if (lane == 0) {
+      const float logit = f64_to(dot + bias, gate_dt);
+      w_out[t] = width_from_logit(logit, gate_dt, n_min, n_max);
+      if (logit_out) logit_out[t] = logit;
+      float xn = sqrtf(__double2float_rn(sq));
+      if (norm_mode == DSALT_NORM_INPUT) xn = round_to(xn, XDT);
+      xnorm_out[t] = xn;
+    }
+#pragma unroll
+    for (int j = 0; j < VCM; ++j) {
+      if (j < vc) {
+        float vv[VN];
+        Vec<VDT>::unpack(vq[j], vv);
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < VN; ++i) s = __fma_rn((double)vv[i], (double)vv[i], s);
+        for (int o = vcpg >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const int c = lane + 32 * j;
+        if ((c % vcpg) == 0) {
+          float vn = sqrtf(__double2float_rn(s));
+          if (norm_mode == DSALT_NORM_INPUT) vn = round_to(vn, VDT);
+          vnorm_out[t * n_kv + c / vcpg] = vn;
+        }
+      }
+    }
+  }
+}
+
 static bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 
 int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride, const void* gate_w,
@@ -181,6 +300,30 @@ int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int
   const int threads = 256;
   int64_t blocks = (T + 7) / 8;
   if (blocks > 148 * 8) blocks = 148 * 8;
+  // wide path: 16-bit x and v, rows in whole 512-byte warp chunks (at most 8 per lane)
+  const int xc = d_model / xvec, vcpg = head_dim / vvec, vtot = n_kv * vcpg;
+  if (xes == 2 && x_dtype == v_dtype && xc % 32 == 0 && xc / 32 <= 8 && vcpg <= 32 && vtot % 32 == 0 &&
+      vtot / 32 <= 8 && d_model <= 6144) {
+    const size_t smem = (size_t)d_model * sizeof(double);
+    const bool x4 = xc / 32 <= 4, v4 = vtot / 32 <= 4;
+#define DSALT_SIG_WIDE(DT, XC, VC)                                                                                 \
+  token_signals_wide_kernel<DT, DT, XC, VC><<<(unsigned)blocks, threads, smem, stream>>>(                          \
+      x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_stride, n_kv, head_dim, norm_mode, \
+      w_out, xnorm_out, vnorm_out, logit_out)
+    if (x_dtype == DSALT_BF16) {
+      if (x4 && v4) DSALT_SIG_WIDE(DSALT_BF16, 4, 4);
+      else if (x4) DSALT_SIG_WIDE(DSALT_BF16, 4, 8);
+      else if (v4) DSALT_SIG_WIDE(DSALT_BF16, 8, 4);
+      else DSALT_SIG_WIDE(DSALT_BF16, 8, 8);
+    } else {
+      if (x4 && v4) DSALT_SIG_WIDE(DSALT_F16, 4, 4);
+      else if (x4) DSALT_SIG_WIDE(DSALT_F16, 4, 8);
+      else if (v4) DSALT_SIG_WIDE(DSALT_F16, 8, 4);
+      else DSALT_SIG_WIDE(DSALT_F16, 8, 8);
+    }
+#undef DSALT_SIG_WIDE
+    return check_cuda(cudaGetLastError(), "token_signals launch");
+  }
 #define DSALT_SIG_LAUNCH(XD, VD)                                                                                   \
   token_signals_kernel<XD, VD><<<(unsigned)blocks, threads, 0, stream>>>(                                          \
       x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_stride, n_kv, head_dim, norm_mode, \
