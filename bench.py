@@ -14,8 +14,9 @@ ranks), ``e2e`` the same metric through the C-ABI call with host buffers (pinned
 host→device copies of x, q, k, v and the device→host copy of the output inside the
 timed region), ``roofline`` the attention kernel's achieved HBM bandwidth against
 MEASURED_PEAKS.json, ``cpu_baseline`` the reference's CPU path on a bounded sample.
-With N > 1 every rank runs its own L=131072 instance (independent replicas, weak
-scaling) — the sequence-sharded path is reported separately.
+With N > 1 (torchrun, one rank per GPU) the same L=131072 sequence is split across the
+ranks (``dsalt_b200.sharded``): strong scaling, ``value`` = L tokens per max-over-ranks
+step time.
 """
 from __future__ import annotations
 
@@ -224,6 +225,114 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_sharded(args, rank, world, local, dev):
+    """N > 1: the L = 131072 sequence split across the ranks (dsalt_b200.sharded): each rank
+    owns L/N queries, signals are all-gathered, landmark rows are read from their owners over
+    NVLink, the window halo comes from the previous rank. Strong scaling: the whole job
+    processes the same L tokens per step as one GPU."""
+    from dsalt_b200 import ops
+    from dsalt_b200.sharded import ShardedCore
+    T, H, D, k, B = CFG["L"], CFG["H"], CFG["D"], CFG["k"], CFG["block"]
+    x, gw, gb, alpha, q, kk, v = make_inputs(dev, seed=0)  # the same sequence on every rank
+    core = ShardedCore(T, H, H, D, k, CFG["n_min"], CFG["n_max"], B)
+    p = core.plan
+    sl = slice(p.q_pos0, p.q_pos0 + p.t_local)
+    xs, qs = x[sl].contiguous(), q[sl].contiguous()
+    core.k_local.copy_(kk[sl])
+    core.v_local.copy_(v[sl])
+    del x, q
+    torch.cuda.synchronize()
+
+    def step():
+        core.forward(xs, gw, gb, alpha, qs)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    status = ops.device_status()
+
+    # dominant kernel: this rank's attention alone
+    w, xn, vn = None, None, None
+    out, lmk = core.forward(xs, gw, gb, alpha, qs)
+    from dsalt_b200.sharded import gather_signals
+    w, xn, vn = gather_signals(core._w, core._xn, core._vn, core.group)
+    n_att = max(20, args.steps // 4)
+    for _ in range(3):
+        ops.attention_sharded(qs, core.k_ext, core.v_ext, p.q_pos0, p.kv_pos0, T, w, lmk, B, core.k_src, core.v_src,
+                              p.t_local, out=core.out)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(n_att):
+        ops.attention_sharded(qs, core.k_ext, core.v_ext, p.q_pos0, p.kv_pos0, T, w, lmk, B, core.k_src, core.v_src,
+                              p.t_local, out=core.out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    att_ms = max_over_ranks(e0.elapsed_time(e1) / n_att, world)
+    att_bytes = 4 * p.t_local * H * D * 2
+    hbm, src = peaks()
+    achieved = att_bytes / (att_ms / 1e3) / 1e9
+    barrier(world)
+
+    # end to end: the shard's inputs from pinned host memory, the shard's output back
+    xh, qh = xs.cpu().pin_memory(), qs.cpu().pin_memory()
+    kh, vh = core.k_local.cpu().pin_memory(), core.v_local.cpu().pin_memory()
+    oh = torch.empty_like(core.out, device="cpu").pin_memory()
+
+    def e2e_step():
+        xs.copy_(xh, non_blocking=True)
+        qs.copy_(qh, non_blocking=True)
+        core.k_local.copy_(kh, non_blocking=True)
+        core.v_local.copy_(vh, non_blocking=True)
+        o, _ = core.forward(xs, gw, gb, alpha, qs)
+        oh.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps, world)
+    h2d = world * sum(t.numel() * t.element_size() for t in (xh, qh, kh, vh))
+    d2h = world * oh.numel() * oh.element_size()
+    if rank == 0:
+        line = {"metric": METRIC, "value": T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": CFG["workload"], "L": T, "heads": H, "head_dim": D, "d_model": CFG["dm"],
+                           "k_lmk": k, "block": B, "n_min": CFG["n_min"], "n_max": CFG["n_max"],
+                           "selection": "block_causal", "l2": "inputs larger than L2",
+                           "parallelism": f"sequence-sharded x{world} (NCCL all-gather of signals, halo send/recv, "
+                                          f"landmark rows over NVLink peer memory)"},
+                "clocks": clk.summary(), "device_status": status,
+                "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "roofline": {"bound": "hbm", "kernel": "attn_fwd_tc_kernel (one rank's shard)", "achieved": achieved,
+                             "peak": hbm, "peak_source": src, "unit": "GB/s", "frac": achieved / hbm,
+                             "traffic": None, "algorithmic_bytes": att_bytes, "kernel_ms": att_ms},
+                "gpu_launches": 11 * args.steps}
+        print(json.dumps(line), flush=True)
+    core.close()
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -244,6 +353,8 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        return run_sharded(args, rank, world, local, dev)
     from dsalt_b200 import ops
     T, H, D, k, B = CFG["L"], CFG["H"], CFG["D"], CFG["k"], CFG["block"]
     x, gw, gb, alpha, q, kk, v = make_inputs(dev, seed=rank)
@@ -324,7 +435,7 @@ def main():
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": CFG["workload"], "L": T, "heads": H, "head_dim": D, "d_model": CFG["dm"],
                            "k_lmk": k, "block": B, "n_min": CFG["n_min"], "n_max": CFG["n_max"],

@@ -69,7 +69,14 @@ struct Params {
   int n_seqs;
   const int32_t* set_base;
   const int32_t* tile_base;
-  const int4* plan;  // per query tile: {start, L, m0, set}, {kstart, nwt, -, -}
+  const int4* plan;  // per query tile: {q row base, L, m0, set}, {kstart, nwt, kv row base, w base}
+  // Sharded mode (shard_tiles > 0): the local query tiles cover positions q_pos0 + 128 t of
+  // one sequence; landmark rows come from the per-rank tables lmk_k_src / lmk_v_src (rank
+  // = position / rows_per_src, possibly another GPU's memory read over NVLink).
+  int shard_tiles, n_sets_local;
+  const uint16_t* const* lmk_k_src;
+  const uint16_t* const* lmk_v_src;
+  int rows_per_src;
   float scale_log2;  // log2(e) / sqrt(head_dim)
   float inv_scale;   // sqrt(head_dim): landmark bias in raw-logit units
   uint32_t idesc_qk, idesc_pv;
@@ -79,8 +86,10 @@ struct Params {
   int* err;
 };
 
+// positions are within the sequence; buffer row of position i: qb + i (q, out),
+// kvb + i (k, v windows and packed landmarks); width of position i: w[wb + i]
 struct Item {
-  int start, L, m0, h, hk, kstart, nwt, nlt, set, n_sets;
+  int qb, kvb, wb, L, m0, h, hk, kstart, nwt, nlt, set, n_sets;
 };
 
 __device__ __forceinline__ int find_seq(const int32_t* base, int n, int idx) {
@@ -97,26 +106,43 @@ __device__ __forceinline__ int find_seq(const int32_t* base, int n, int idx) {
 // window needs. Window tiles end at the tile's last row, so that the last one holds
 // every row's diagonal key; the first may start before the sequence (those keys are
 // masked). Replaces _build_seq_block_map (selectors.py:37-67).
+// Sharded mode (shard_tiles > 0): tile t is positions q_pos0 + 128 t of one sequence of
+// length seq_len, q/out row = position - q_pos0, k/v row = position - kv_pos0, widths
+// indexed by position, landmark set = position / lmk_block - set_lo.
 __global__ void tile_plan_kernel(const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ tile_base,
                                  const int32_t* __restrict__ set_base, int lmk_block, const int32_t* __restrict__ w,
-                                 int4* __restrict__ plan) {
+                                 int4* __restrict__ plan, int shard_tiles, int q_pos0, int kv_pos0, int seq_len,
+                                 int set_lo) {
   const int tile = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (tile >= tile_base[n_seqs]) return;
-  const int s = find_seq(tile_base, n_seqs, tile);
-  const int start = cu[s], L = cu[s + 1] - start;
-  const int m0 = (tile - tile_base[s]) * BM;
+  int qb, kvb, wb, L, m0, set;
+  if (shard_tiles > 0) {
+    if (tile >= shard_tiles) return;
+    qb = -q_pos0;
+    kvb = -kv_pos0;
+    wb = 0;
+    L = seq_len;
+    m0 = q_pos0 + tile * BM;
+    set = lmk_block ? m0 / lmk_block - set_lo : 0;
+  } else {
+    if (tile >= tile_base[n_seqs]) return;
+    const int s = find_seq(tile_base, n_seqs, tile);
+    qb = kvb = wb = cu[s];
+    L = cu[s + 1] - qb;
+    m0 = (tile - tile_base[s]) * BM;
+    set = lmk_block ? set_base[s] + m0 / lmk_block : s;
+  }
   int wm = 1;
   for (int r = lane; r < BM; r += 32)
-    if (m0 + r < L) wm = max(wm, __ldg(w + start + m0 + r));
+    if (m0 + r < L) wm = max(wm, __ldg(w + wb + m0 + r));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, o));
   const int hi = min(m0 + BM - 1, L - 1);
   const int kmin = max(0, m0 - wm + 1);
   const int nwt = (hi - kmin + BN) / BN;
   if (lane == 0) {
-    plan[2 * tile] = make_int4(start, L, m0, lmk_block ? set_base[s] + m0 / lmk_block : s);
-    plan[2 * tile + 1] = make_int4(hi + 1 - nwt * BN, nwt, 0, 0);
+    plan[2 * tile] = make_int4(qb, L, m0, set);
+    plan[2 * tile + 1] = make_int4(hi + 1 - nwt * BN, nwt, kvb, wb);
   }
 }
 
@@ -125,12 +151,14 @@ __device__ __forceinline__ Item make_item(const Params& p, int item, int4 a, int
   const int tile = item / p.H;
   f.h = item - tile * p.H;
   f.hk = f.h / (p.H / p.Hkv);
-  f.start = a.x;
+  f.qb = a.x;
   f.L = a.y;
   f.m0 = a.z;
   f.set = a.w;
   f.kstart = b.x;
   f.nwt = b.y;
+  f.kvb = b.z;
+  f.wb = b.w;
   f.nlt = (p.k_lmk + BN - 1) / BN;
   f.n_sets = n_sets;
   return f;
@@ -243,7 +271,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + SM::MISC_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = p.tile_base[p.n_seqs] * p.H;
+  const int n_items = (p.shard_tiles > 0 ? p.shard_tiles : p.tile_base[p.n_seqs]) * p.H;
 
   if (threadIdx.x == 0) {
     for (int pp = 0; pp < NPIPE; ++pp) {
@@ -312,7 +340,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       const uint16_t* kg = reinterpret_cast<const uint16_t*>(p.k);
       const uint16_t* vg = reinterpret_cast<const uint16_t*>(p.v);
-      const int n_sets = p.lmk_block ? __ldg(p.set_base + p.n_seqs) : p.n_seqs;
+      const int n_sets = p.shard_tiles > 0 ? p.n_sets_local : p.lmk_block ? __ldg(p.set_base + p.n_seqs) : p.n_seqs;
       // Publish item `item_n` (the it_n-th of this pipeline) into its slot: the description
       // from the tile plan (a, b), then the rows' window widths and the landmark positions
       // by cp.async; the slot is full when the copies have landed.
@@ -326,7 +354,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int c = lane; c < p.k_lmk; c += 32) cp_async_4(smem_u32(&S.pos[c]), P + c, 4u);
         for (int r = lane; r < BM; r += 32) {
           const bool vrow = fn.m0 + r < fn.L;
-          cp_async_4(smem_u32(&S.wv[r]), p.w + fn.start + (vrow ? fn.m0 + r : 0), vrow ? 4u : 0u);
+          cp_async_4(smem_u32(&S.wv[r]), p.w + fn.wb + (vrow ? fn.m0 + r : 0), vrow ? 4u : 0u);
         }
         cp_async_mbar_arrive(&B.it_full[sl]);
         __syncwarp();
@@ -358,17 +386,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mbar_arrive_expect_tx(&B.q_full[qb], SM::TILE_BYTES);
           for (int a = 0; a < SM::NA; ++a)
             tma_load_3d(pbase + SM::Q_OFF + qb * SM::TILE_BYTES + a * BM * 128, &tm_q, &B.q_full[qb], a * 64, f.h,
-                        f.start + f.m0);
+                        f.qb + f.m0);
         }
         const int NK = f.nwt + f.nlt;
         // the landmark rows are gathered after the window tiles: bring them into L2 now
         // (scattered 128-byte rows; the gather would otherwise wait on DRAM latency)
-        if (f.nlt > 0) {
+        if (f.nlt > 0 && p.shard_tiles == 0) {
           if (!mbar_wait(&B.it_full[sl_i], (uint32_t)(it / NIS) & 1, p.err, 15)) break;
           for (int c = lane; c < p.k_lmk; c += 32) {
             const int pos = S.pos[c];
             if (pos >= 0) {
-              const int64_t off = (int64_t)(f.start + pos) * p.kv_stride + (int64_t)f.hk * HD;
+              const int64_t off = (int64_t)(f.kvb + pos) * p.kv_stride + (int64_t)f.hk * HD;
               prefetch_l2(kg + off);
               prefetch_l2(vg + off);
             }
@@ -384,7 +412,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t kdst = pbase + SM::K_OFF + sk * SM::TILE_BYTES;
           const uint32_t vdst = pbase + SM::V_OFF + sv * SM::TILE_BYTES;
           if (jt >= 0) {
-            const int row = f.start + f.kstart + jt * BN;
+            const int row = f.kvb + f.kstart + jt * BN;
             if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
             if (lane == 0) {
               mbar_arrive_expect_tx(&B.k_full[sk], SM::TILE_BYTES);
@@ -414,11 +442,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int rr = j * RPI + rsub;
                 const int idx = lt * BN + rb + rr;
                 const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
-                const int64_t off = (int64_t)(f.start + (pos < 0 ? 0 : pos)) * p.kv_stride + head_off;
+                const int pc = pos < 0 ? 0 : pos;
+                const uint16_t *ks, *vs;
+                int64_t row;
+                if (p.shard_tiles > 0) {
+                  const int src = pc / p.rows_per_src;
+                  ks = p.lmk_k_src[src];
+                  vs = p.lmk_v_src[src];
+                  row = pc - (int64_t)src * p.rows_per_src;
+                } else {
+                  ks = kg;
+                  vs = vg;
+                  row = (int64_t)f.kvb + pc;
+                }
+                const int64_t off = row * p.kv_stride + head_off;
                 const uint32_t so = swz_off<HD>(rb + rr, c);
                 const uint32_t nb = pos < 0 ? 0u : 16u;
-                cp_async_16(kdst + so, kg + off, nb);
-                cp_async_16(vdst + so, vg + off, nb);
+                cp_async_16(kdst + so, ks + off, nb);
+                cp_async_16(vdst + so, vs + off, nb);
               }
             }
             cp_async_wait_all();
@@ -728,7 +769,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (vrow) {
         const bool good = l > 1e-9f;
         const float inv = good ? 1.0f / l : 0.0f;
-        const int64_t row = (int64_t)(f.start + i);
+        const int64_t row = (int64_t)f.qb + i;
         if (p.out_dtype == DSALT_F32) {
           float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (row * p.H + f.h) * HD);
 #pragma unroll
@@ -797,7 +838,7 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
                    int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, int32_t* set_base, int32_t* tile_base,
                    int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const ShardArgs* shard) {
   using namespace tc;
   if (HD != 64) return fail(DSALT_ERR_UNSUPPORTED, "attention (tensor cores): head_dim %d not supported (64)", HD);
   if (k_lmk > MAX_LMK) return fail(DSALT_ERR_UNSUPPORTED, "attention: k_lmk %d above %d", k_lmk, MAX_LMK);
@@ -805,15 +846,24 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15 || (q_stride * 2) % 16 ||
       (kv_stride * 2) % 16)
     return fail(DSALT_ERR_INVALID, "attention: q/k/v/out must be 16-byte aligned with 16-byte row strides");
+  // q/out rows: T (packed) or the shard's query rows; k/v rows: T or the shard's key rows
+  const int64_t q_rows = shard ? shard->q_rows : T, kv_rows = shard ? shard->kv_rows : T;
   CUtensorMap mq, mk, mv;
   int rc;
-  if ((rc = make_map(&mq, q, dtype, HD, H, T, q_stride))) return rc;
-  if ((rc = make_map(&mk, k, dtype, HD, Hkv, T, kv_stride))) return rc;
-  if ((rc = make_map(&mv, v, dtype, HD, Hkv, T, kv_stride))) return rc;
-  if ((rc = launch_chunk_table(cu, n_seqs, BM, tile_base, stream))) return rc;
-  if (lmk_block > 0 && (rc = launch_chunk_table(cu, n_seqs, lmk_block, set_base, stream))) return rc;
-  tile_plan_kernel<<<(unsigned)((max_tiles + 7) / 8), 256, 0, stream>>>(cu, n_seqs, tile_base, set_base, lmk_block, w,
-                                                                       plan);
+  if ((rc = make_map(&mq, q, dtype, HD, H, q_rows, q_stride))) return rc;
+  if ((rc = make_map(&mk, k, dtype, HD, Hkv, kv_rows, kv_stride))) return rc;
+  if ((rc = make_map(&mv, v, dtype, HD, Hkv, kv_rows, kv_stride))) return rc;
+  const int shard_tiles = shard ? (int)(shard->q_rows / BM) : 0;
+  if (shard) {
+    tile_plan_kernel<<<(unsigned)((shard_tiles + 7) / 8), 256, 0, stream>>>(
+        cu, n_seqs, tile_base, set_base, lmk_block, w, plan, shard_tiles, (int)shard->q_pos0, (int)shard->kv_pos0,
+        (int)shard->seq_len, lmk_block ? (int)(shard->q_pos0 / lmk_block) : 0);
+  } else {
+    if ((rc = launch_chunk_table(cu, n_seqs, BM, tile_base, stream))) return rc;
+    if (lmk_block > 0 && (rc = launch_chunk_table(cu, n_seqs, lmk_block, set_base, stream))) return rc;
+    tile_plan_kernel<<<(unsigned)((max_tiles + 7) / 8), 256, 0, stream>>>(cu, n_seqs, tile_base, set_base, lmk_block,
+                                                                         w, plan, 0, 0, 0, 0, 0);
+  }
   if ((rc = check_cuda(cudaGetLastError(), "tile plan launch"))) return rc;
   Params p{};
   p.k = k;
@@ -831,6 +881,13 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   p.set_base = set_base;
   p.tile_base = tile_base;
   p.plan = plan;
+  if (shard) {
+    p.shard_tiles = shard_tiles;
+    p.n_sets_local = lmk_block ? (int)((shard->q_rows + lmk_block - 1) / lmk_block) : 1;
+    p.lmk_k_src = reinterpret_cast<const uint16_t* const*>(shard->lmk_k_src);
+    p.lmk_v_src = reinterpret_cast<const uint16_t* const*>(shard->lmk_v_src);
+    p.rows_per_src = (int)shard->rows_per_src;
+  }
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
   p.inv_scale = (float)sqrt((double)HD);
   const uint32_t ab = dtype == DSALT_BF16 ? 1u : 0u;
@@ -843,7 +900,7 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t max_items = (T / BM + n_seqs) * (int64_t)H;
+  const int64_t max_items = (shard ? (int64_t)shard_tiles : T / BM + n_seqs) * (int64_t)H;
   const int64_t want = (max_items + NPIPE - 1) / NPIPE;
   const int grid = (int)(want < nsm ? want : nsm);
   if (grid <= 0) return DSALT_OK;

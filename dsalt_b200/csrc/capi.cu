@@ -6,6 +6,8 @@
 
 #include <mutex>
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace dsalt {
@@ -19,7 +21,11 @@ size_t select_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, i
 int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
                   const int32_t* cu, int n_seqs, int64_t T, int max_seqlen, int n_heads, int n_kv, int k, int block,
                   int32_t* lmk_out, float* zx_out, float* zv_out, void* workspace, size_t ws_bytes,
-                  cudaStream_t stream);
+                  cudaStream_t stream, int set_lo = 0, int set_hi = -1);
+size_t select_range_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block, int set_hi);
+int launch_select_range(const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha, int64_t seq_len,
+                        int n_heads, int n_kv, int k, int block, int set_lo, int set_hi, int32_t* lmk_out,
+                        void* workspace, size_t ws_bytes, cudaStream_t stream);
 int select_set_up_attributes();
 int launch_attn_f32(const float* q, const float* k, const float* v, int64_t T, int H, int Hkv, int D,
                     int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
@@ -29,7 +35,7 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
                    int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, int32_t* set_base, int32_t* tile_base,
                    int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
-                   cudaStream_t stream);
+                   cudaStream_t stream, const ShardArgs* shard = nullptr);
 int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream);
 
 // ---------------------------------------------------------------- errors
@@ -187,6 +193,103 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
   return launch_attn_tc(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
                         lmk_block, cu_seqlens, n_seqs, set_base, tile_base, plan, attention_max_tiles(T, n_seqs), out,
                         out_dtype, lse, device_status_ptr(), s);
+}
+
+size_t dsalt_select_block_range_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block,
+                                                int set_hi) {
+  return select_range_workspace_bytes(seq_len, n_heads, n_kv, k, block, set_hi);
+}
+
+int dsalt_select_block_range(const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                             int64_t seq_len, int n_heads, int n_kv, int k, int block, int set_lo, int set_hi,
+                             int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (n_heads < 1 || n_kv < 1 || n_heads % n_kv || k < 0) return fail(DSALT_ERR_INVALID, "select range: bad sizes");
+  if (!xnorm || !vnorm || !w || !alpha || !lmk_out) return fail(DSALT_ERR_INVALID, "select range: null pointer");
+  if (seq_len > 0x7fffff00LL) return fail(DSALT_ERR_UNSUPPORTED, "select range: sequence too long");
+  return launch_select_range(xnorm, vnorm, w, alpha, seq_len, n_heads, n_kv, k, block, set_lo, set_hi, lmk_out,
+                             workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dsalt_attention_sharded_workspace_bytes(int64_t q_rows, int n_heads) {
+  (void)n_heads;
+  if (q_rows < 0) return 0;
+  return 256 + a256(32 * (size_t)(q_rows / 128 + 1));
+}
+
+int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int dtype, int64_t q_rows, int n_heads,
+                                int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, int64_t q_pos0,
+                                int64_t kv_pos0, int64_t kv_rows, int64_t seq_len, const int32_t* w,
+                                const int32_t* lmk, const float* lmk_bias, int k_lmk, int lmk_block,
+                                const void* const* lmk_k_src, const void* const* lmk_v_src, int64_t rows_per_src,
+                                void* out, int out_dtype, float* lse, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (q_rows < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || head_dim < 1 || k_lmk < 0 || lmk_block < 0 ||
+      kv_rows < 0 || rows_per_src < 1)
+    return fail(DSALT_ERR_INVALID, "attention (sharded): bad sizes");
+  if (dtype != DSALT_BF16 && dtype != DSALT_F16)
+    return fail(DSALT_ERR_UNSUPPORTED, "attention (sharded): bf16 / fp16 inputs only");
+  if (!valid_dtype(out_dtype)) return fail(DSALT_ERR_INVALID, "attention (sharded): dtype");
+  if (q_rows == 0) return DSALT_OK;
+  if (q_pos0 % 128 || q_rows % 128 || (lmk_block && q_pos0 % lmk_block))
+    return fail(DSALT_ERR_UNSUPPORTED, "attention (sharded): shard must start and end on 128-query (and set) bounds");
+  if (q_pos0 < 0 || kv_pos0 > q_pos0 || kv_pos0 + kv_rows < q_pos0 + q_rows || q_pos0 + q_rows > seq_len ||
+      seq_len > 0x7fffff00LL)
+    return fail(DSALT_ERR_INVALID, "attention (sharded): k/v rows must cover the shard's own positions");
+  if (q_stride < (int64_t)n_heads * head_dim || kv_stride < (int64_t)n_kv * head_dim)
+    return fail(DSALT_ERR_INVALID, "attention (sharded): token stride smaller than heads x head_dim");
+  if (!q || !k || !v || !w || !out || (k_lmk > 0 && (!lmk || !lmk_k_src || !lmk_v_src)) || !workspace)
+    return fail(DSALT_ERR_INVALID, "attention (sharded): null pointer");
+  const size_t need = dsalt_attention_sharded_workspace_bytes(q_rows, n_heads);
+  if (workspace_bytes < need)
+    return fail(DSALT_ERR_WORKSPACE, "attention (sharded): workspace %zu < %zu", workspace_bytes, need);
+  ShardArgs sa{q_pos0, q_rows, kv_pos0, kv_rows, seq_len, rows_per_src, lmk_k_src, lmk_v_src};
+  int4* plan = reinterpret_cast<int4*>(reinterpret_cast<char*>(workspace) + 256);
+  int32_t* tables = reinterpret_cast<int32_t*>(workspace);
+  return launch_attn_tc(q, k, v, dtype, q_rows, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
+                        lmk_block, nullptr, 1, tables, tables + 32, plan, q_rows / 128, out, out_dtype, lse,
+                        device_status_ptr(), reinterpret_cast<cudaStream_t>(stream), &sa);
+}
+
+// device memory shared between the processes of one node (CUDA IPC, plain peer mappings)
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int dsalt_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out) return fail(DSALT_ERR_INVALID, "ipc export: null pointer");
+  static GetAddressRangeFn range_fn = nullptr;
+  if (!range_fn) {
+    void* fp = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fp, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(DSALT_ERR_CUDA, "ipc export: cuMemGetAddressRange unavailable");
+    range_fn = reinterpret_cast<GetAddressRangeFn>(fp);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, (CUdeviceptr)ptr) != CUDA_SUCCESS)
+    return fail(DSALT_ERR_CUDA, "ipc export: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  int rc = check_cuda(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)), "ipc export");
+  if (rc) return rc;
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = (int64_t)((CUdeviceptr)ptr - base);
+  return DSALT_OK;
+}
+
+int dsalt_ipc_open(const void* handle, int64_t offset, void** ptr_out) {
+  if (!handle || !ptr_out) return fail(DSALT_ERR_INVALID, "ipc open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  int rc = check_cuda(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess), "ipc open");
+  if (rc) return rc;
+  *ptr_out = reinterpret_cast<char*>(base) + offset;
+  return DSALT_OK;
+}
+
+int dsalt_ipc_close(void* ptr, int64_t offset) {
+  if (!ptr) return fail(DSALT_ERR_INVALID, "ipc close: null pointer");
+  return check_cuda(cudaIpcCloseMemHandle(reinterpret_cast<char*>(ptr) - offset), "ipc close");
 }
 
 // Callers without a device allocator (bindings that hold only the caller's pointers,

@@ -14,6 +14,16 @@
 
 namespace dsalt {
 
+// One rank's share of a sequence-sharded attention call (see dsalt_attention_fwd_sharded):
+// q/out rows are positions [q_pos0, q_pos0 + q_rows) of one sequence of seq_len positions,
+// k/v rows are positions [kv_pos0, kv_pos0 + kv_rows); landmark row of position p is row
+// p - r * rows_per_src of rank r = p / rows_per_src's K/V (device arrays of pointers).
+struct ShardArgs {
+  int64_t q_pos0, q_rows, kv_pos0, kv_rows, seq_len, rows_per_src;
+  const void* const* lmk_k_src;
+  const void* const* lmk_v_src;
+};
+
 // --------------------------------------------------------------------------
 // host-side error reporting (set by the C-ABI entry points)
 // --------------------------------------------------------------------------

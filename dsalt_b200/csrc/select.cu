@@ -22,6 +22,8 @@
 // inputs). Heads whose α is outside [0,1] skip the pruning.
 #include <math.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace dsalt {
@@ -613,7 +615,8 @@ __global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w,
     const float* __restrict__ alpha, const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base,
     int C, int n_heads, int n_kv, int k, const double2* __restrict__ stats, const int32_t* __restrict__ D,
-    const int32_t* __restrict__ surv_cnt, const int4* __restrict__ surv_rec, int32_t* __restrict__ lmk_out) {
+    const int32_t* __restrict__ surv_cnt, const int4* __restrict__ surv_rec, int32_t* __restrict__ lmk_out, int set_lo,
+    int n_out) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
   __shared__ TopkSmem sm;
@@ -622,10 +625,11 @@ __global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
   __shared__ int32_t wsum[32];
   __shared__ int32_t dsm[NCELL];
   __shared__ int32_t ncand;
-  const int c = blockIdx.x, h = blockIdx.y;
+  // sets set_lo + blockIdx.x; output [H, n_out, k] (n_out = all sets, or the range's)
+  const int c = set_lo + blockIdx.x, h = blockIdx.y;
   const int total = base[n_seqs];
   if (c >= total) return;
-  int32_t* out = lmk_out + ((int64_t)h * total + c) * k;  // [H, n_sets, k], n_sets = total
+  int32_t* out = lmk_out + ((int64_t)h * (n_out > 0 ? n_out : total) + (c - set_lo)) * k;
   const int s = find_seq(base, n_seqs, c);
   const int b = c - base[s];
   const int n = b * C;
@@ -817,7 +821,7 @@ int select_set_up_attributes();
 int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
                   const int32_t* cu, int n_seqs, int64_t T, int max_seqlen, int n_heads, int n_kv, int k, int block,
                   int32_t* lmk_out, float* zx_out, float* zv_out, void* workspace, size_t ws_bytes,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, int set_lo, int set_hi) {
   if (mode != DSALT_SELECT_GLOBAL && mode != DSALT_SELECT_BLOCK_CAUSAL) return fail(DSALT_ERR_INVALID, "select: mode");
   if (n_seqs < 1 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || T < 0 || k < 0)
     return fail(DSALT_ERR_INVALID, "select: bad sizes");
@@ -868,10 +872,48 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
     survivor_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges,
                                                                   G, k, cnt, recs);
     const size_t sm3 = sizeof(uint64_t) * KEY_CAP;
-    block_select_kernel<<<dim3(L.max_chunks, n_heads), SEL_THREADS, sm3, stream>>>(
-        xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, G, cnt, recs, lmk_out);
+    const bool range = set_hi >= 0;
+    block_select_kernel<<<dim3(range ? set_hi - set_lo : L.max_chunks, n_heads), SEL_THREADS, sm3, stream>>>(
+        xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, G, cnt, recs, lmk_out,
+        range ? set_lo : 0, range ? set_hi - set_lo : 0);
   }
   return check_cuda(cudaGetLastError(), "select launch");
+}
+
+__global__ void prefix_cu_kernel(int32_t* cu, int T) {
+  if (threadIdx.x == 0) {
+    cu[0] = 0;
+    cu[1] = T;
+  }
+}
+
+// Block-causal sets [set_lo, set_hi) of one sequence whose signals cover positions
+// [0, seq_len): only the prefix [0, set_hi * block) is read (later tokens cannot be
+// landmarks of these blocks). Workspace: the selection workspace of that prefix + 256 B.
+size_t select_range_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block, int set_hi) {
+  if (block <= 0 || set_hi < 0) return 0;
+  const int64_t Tp = std::min<int64_t>(seq_len, (int64_t)set_hi * block);
+  return 256 + select_workspace_bytes(DSALT_SELECT_BLOCK_CAUSAL, Tp, 1, (int)Tp, n_heads, n_kv, k, block);
+}
+
+int launch_select_range(const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha, int64_t seq_len,
+                        int n_heads, int n_kv, int k, int block, int set_lo, int set_hi, int32_t* lmk_out,
+                        void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  if (block < 32 || block > 1024 || block % 32) return fail(DSALT_ERR_UNSUPPORTED, "select range: block");
+  if (seq_len < 0 || set_lo < 0 || set_hi < set_lo || (int64_t)set_hi * block > seq_len + block - 1)
+    return fail(DSALT_ERR_INVALID, "select range: sets [%d, %d) outside a sequence of %lld", set_lo, set_hi,
+                (long long)seq_len);
+  if (set_hi == set_lo || k == 0) return DSALT_OK;
+  const size_t need = select_range_workspace_bytes(seq_len, n_heads, n_kv, k, block, set_hi);
+  if (!workspace || ws_bytes < need) return fail(DSALT_ERR_WORKSPACE, "select range: workspace %zu < %zu", ws_bytes, need);
+  const int64_t Tp = std::min<int64_t>(seq_len, (int64_t)set_hi * block);
+  int32_t* cu = reinterpret_cast<int32_t*>(workspace);
+  prefix_cu_kernel<<<1, 32, 0, stream>>>(cu, (int)Tp);
+  int rc = check_cuda(cudaGetLastError(), "select range setup");
+  if (rc) return rc;
+  return launch_select(DSALT_SELECT_BLOCK_CAUSAL, xnorm, vnorm, w, alpha, cu, 1, Tp, (int)Tp, n_heads, n_kv, k, block,
+                       lmk_out, nullptr, nullptr, reinterpret_cast<char*>(workspace) + 256, ws_bytes - 256, stream,
+                       set_lo, set_hi);
 }
 
 int select_set_up_attributes() {

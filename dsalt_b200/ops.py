@@ -274,3 +274,71 @@ def device_status(clear: bool = True) -> int:
 
 def scale_for(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+# --------------------------------------------------------------------------- sequence shards
+def select_block_range(xnorm, vnorm, w, alpha, k_lmk: int, n_heads: int, block: int, set_lo: int, set_hi: int,
+                       workspace=None):
+    """Block-causal landmark sets ``[set_lo, set_hi)`` of one sequence whose per-position
+    signals (``xnorm [L]``, ``vnorm [L, n_kv]``, ``w [L]``) are all given (``dsalt_select_block_range``).
+    Returns ``[n_heads, set_hi - set_lo, k_lmk]`` int32, the same sets as
+    :func:`select_landmarks` in ``block_causal`` mode."""
+    _cuda(xnorm, vnorm, w, alpha)
+    Lseq = xnorm.shape[0]
+    n_kv = vnorm.shape[1]
+    out = torch.empty(n_heads, set_hi - set_lo, k_lmk, dtype=torch.int32, device=xnorm.device)
+    n = L.query("dsalt_select_block_range_workspace_bytes", Lseq, n_heads, n_kv, k_lmk, block, set_hi)
+    ws = workspace if workspace is not None and workspace.numel() >= n else _workspace(n, xnorm.device)
+    L.call("dsalt_select_block_range", _ptr(xnorm.contiguous()), _ptr(vnorm.contiguous()),
+           _ptr(w.to(torch.int32).contiguous()), _ptr(alpha.float().contiguous()), Lseq, n_heads, n_kv, k_lmk, block,
+           set_lo, set_hi, _ptr(out), _ptr(ws), ws.numel(), _stream())
+    return out
+
+
+def attention_sharded(q, k, v, q_pos0: int, kv_pos0: int, seq_len: int, w, lmk, lmk_block: int, lmk_k_src,
+                      lmk_v_src, rows_per_src: int, *, lmk_bias=None, out=None, workspace=None):
+    """One rank's share of a sequence-sharded attention (``dsalt_attention_fwd_sharded``).
+
+    ``q [q_rows, H, D]`` are positions ``[q_pos0, q_pos0 + q_rows)``; ``k, v [kv_rows, H_kv, D]``
+    positions ``[kv_pos0, kv_pos0 + kv_rows)`` (the shard plus its window halo); ``w [seq_len]``;
+    ``lmk [H, n_local_sets, k]`` ascending with -1 last; ``lmk_k_src`` / ``lmk_v_src``: int64
+    device tensors of the ranks' K / V shard base pointers. Returns ``out [q_rows, H, D]``
+    in the input dtype."""
+    _cuda(q, k, v, w, lmk, lmk_k_src, lmk_v_src)
+    q_rows, H, D = q.shape
+    n_kv = k.shape[1]
+    if q.stride(2) != 1 or q.stride(1) != D or k.stride(2) != 1 or k.stride(1) != D or k.stride(0) != v.stride(0):
+        raise ValueError("q, k, v must have contiguous heads and k, v the same token stride")
+    if out is None:
+        out = torch.empty(q_rows, H, D, dtype=q.dtype, device=q.device)
+    n = L.query("dsalt_attention_sharded_workspace_bytes", q_rows, H)
+    ws = workspace if workspace is not None and workspace.numel() >= n else _workspace(n, q.device)
+    bias = None if lmk_bias is None else lmk_bias.float().contiguous()
+    L.call("dsalt_attention_fwd_sharded", _ptr(q), _ptr(k), _ptr(v), _dt(q), q_rows, H, n_kv, D, q.stride(0),
+           k.stride(0), q_pos0, kv_pos0, k.shape[0], seq_len, _ptr(w), _ptr(lmk), _ptr(bias), int(lmk.shape[-1]),
+           int(lmk_block), _ptr(lmk_k_src), _ptr(lmk_v_src), rows_per_src, _ptr(out), _dt(out), None, _ptr(ws),
+           ws.numel(), _stream())
+    return out
+
+
+def ipc_export(t: torch.Tensor):
+    """(64-byte CUDA IPC handle, byte offset) of a CUDA tensor's data pointer."""
+    import ctypes
+    h = (ctypes.c_char * 64)()
+    off = ctypes.c_int64(0)
+    L.call("dsalt_ipc_export", ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off))
+    return bytes(h), int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Device pointer (int) of another process's tensor on this node (plain peer mapping)."""
+    import ctypes
+    p = ctypes.c_void_p(0)
+    buf = ctypes.create_string_buffer(handle, 64)
+    L.call("dsalt_ipc_open", buf, offset, ctypes.byref(p))
+    return int(p.value)
+
+
+def ipc_close(ptr: int, offset: int) -> None:
+    import ctypes
+    L.call("dsalt_ipc_close", ctypes.c_void_p(ptr), offset)

@@ -1,0 +1,190 @@
+"""Sequence-sharded DSALT core (block-causal selection) over the GPUs of one node, one
+process per GPU (``torch.distributed``, NCCL).
+
+One sequence of ``seq_len`` positions is split into contiguous shards of ``T_local``
+positions; rank ``r`` owns queries ``[r·T_local, (r+1)·T_local)`` and computes their
+projections outside this module. Per step:
+
+1. window widths and selection signals of the rank's own tokens (``dsalt_token_signals``);
+2. one NCCL all-gather of those compact signals (``w``, ``‖x‖``, value norms: 4·(2+H_kv)
+   bytes per token), so every rank holds them for the whole sequence;
+3. the block-causal landmark sets of the rank's own 512-query blocks
+   (``dsalt_select_block_range``: block ``b`` uses the prefix ``[0, b·512)``, as
+   ``results/causal_landmark_check.py:176-186``);
+4. the window halo: the previous rank's last ``n_max - 1`` K/V rows, NCCL send/recv into
+   the rows in front of the local shard;
+5. the attention of the local queries (``dsalt_attention_fwd_sharded``): window tiles from
+   the halo-extended local K/V, landmark rows read directly from their owner's K/V shard
+   over NVLink (CUDA IPC peer mappings, plain loads — no multicast);
+6. a closing NCCL all-reduce of one word, so that no rank overwrites its K/V shard while
+   another may still read landmark rows from it.
+
+The output stays sharded (``[T_local, H, D]`` per rank). Results equal the single-GPU
+core on the whole sequence bit for bit (same kernels, same tiles).
+
+The exchange helpers (:func:`shard_plan`, :func:`gather_signals`,
+:func:`exchange_halo`) are device-agnostic and tested with ``gloo`` on CPU.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+import torch.distributed as dist
+
+
+@dataclasses.dataclass(frozen=True)
+class ShardPlan:
+    world: int
+    rank: int
+    seq_len: int
+    t_local: int      # queries per rank
+    q_pos0: int       # first position of the rank's queries
+    halo: int         # K/V rows in front of the shard (keys of earlier ranks)
+    block: int        # selection block (queries per landmark set)
+
+    @property
+    def kv_pos0(self) -> int:
+        return self.q_pos0 - self.halo
+
+    @property
+    def set_lo(self) -> int:
+        return self.q_pos0 // self.block
+
+    @property
+    def set_hi(self) -> int:
+        return (self.q_pos0 + self.t_local) // self.block
+
+
+def shard_plan(seq_len: int, world: int, rank: int, n_max: int, block: int = 512) -> ShardPlan:
+    """Contiguous shards of ``seq_len / world`` positions. Each shard must be a whole
+    number of selection blocks and of 128-query tiles; the halo holds ``n_max - 1`` keys
+    (the widest window reaches ``n_max - 1`` positions back)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad world / rank")
+    if seq_len % world:
+        raise ValueError(f"seq_len {seq_len} is not divisible by {world} ranks")
+    t_local = seq_len // world
+    if t_local % block or t_local % 128:
+        raise ValueError(f"shard of {t_local} positions is not a whole number of {block}-query blocks")
+    q_pos0 = rank * t_local
+    halo = min(q_pos0, max(n_max - 1, 0))
+    return ShardPlan(world, rank, seq_len, t_local, q_pos0, halo, block)
+
+
+def gather_signals(w_loc: torch.Tensor, xn_loc: torch.Tensor, vn_loc: torch.Tensor, group=None):
+    """All-gather the per-token signals of every rank's shard (one collective).
+
+    ``w_loc [T]`` int32, ``xn_loc [T]`` fp32, ``vn_loc [T, H_kv]`` fp32 →
+    ``(w [P·T], xn [P·T], vn [P·T, H_kv])`` in position order."""
+    T = w_loc.shape[0]
+    n_kv = vn_loc.shape[1]
+    flat = torch.empty(T * (2 + n_kv), dtype=torch.int32, device=w_loc.device)
+    flat[:T] = w_loc
+    flat[T:2 * T] = xn_loc.view(torch.int32)
+    flat[2 * T:] = vn_loc.reshape(-1).view(torch.int32)
+    P = dist.get_world_size(group)
+    out = torch.empty(P * flat.numel(), dtype=torch.int32, device=flat.device)
+    dist.all_gather_into_tensor(out, flat, group=group)
+    out = out.view(P, flat.numel())
+    w = out[:, :T].reshape(P * T)
+    xn = out[:, T:2 * T].reshape(P * T).view(torch.float32)
+    vn = out[:, 2 * T:].reshape(P * T, n_kv).view(torch.float32)
+    return w, xn, vn
+
+
+def exchange_halo(k_ext: torch.Tensor, v_ext: torch.Tensor, plan: ShardPlan, halo_next: int, group=None):
+    """Ring exchange of the window halo: the last ``halo_next`` rows of this rank's shard go
+    to rank+1; the previous rank's last ``plan.halo`` rows land in ``k_ext[:plan.halo]``
+    (and likewise for V). ``k_ext`` / ``v_ext`` are ``[halo + T_local, H_kv, D]``."""
+    ops = []
+    r, P = plan.rank, plan.world
+    if r + 1 < P and halo_next > 0:
+        ops.append(dist.P2POp(dist.isend, k_ext[k_ext.shape[0] - halo_next:].contiguous(), r + 1, group))
+        ops.append(dist.P2POp(dist.isend, v_ext[v_ext.shape[0] - halo_next:].contiguous(), r + 1, group))
+    if r > 0 and plan.halo > 0:
+        ops.append(dist.P2POp(dist.irecv, k_ext[:plan.halo], r - 1, group))
+        ops.append(dist.P2POp(dist.irecv, v_ext[:plan.halo], r - 1, group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+
+
+class ShardedCore:
+    """The core of one DSALT layer (widths, block-causal selection, attention) for one
+    rank's shard of a sequence. ``k_local`` / ``v_local`` are the views the caller writes
+    its shard's post-RoPE keys / values into before :meth:`forward`."""
+
+    def __init__(self, seq_len: int, n_heads: int, n_kv: int, head_dim: int, k_lmk: int, n_min: int, n_max: int,
+                 block: int = 512, dtype=torch.bfloat16, group=None):
+        from . import ops
+        self.ops = ops
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.plan = shard_plan(seq_len, self.world, self.rank, n_max, block)
+        nxt = shard_plan(seq_len, self.world, self.rank + 1, n_max, block) if self.rank + 1 < self.world else None
+        self.halo_next = nxt.halo if nxt is not None else 0
+        self.n_heads, self.n_kv, self.head_dim = n_heads, n_kv, head_dim
+        self.k_lmk, self.n_min, self.n_max, self.block = k_lmk, n_min, n_max, block
+        dev = torch.device("cuda", torch.cuda.current_device())
+        p = self.plan
+        self.k_ext = torch.zeros(p.halo + p.t_local, n_kv, head_dim, dtype=dtype, device=dev)
+        self.v_ext = torch.zeros_like(self.k_ext)
+        self.k_local = self.k_ext[p.halo:]
+        self.v_local = self.v_ext[p.halo:]
+        self.out = torch.empty(p.t_local, n_heads, head_dim, dtype=dtype, device=dev)
+        self._w = torch.empty(p.t_local, dtype=torch.int32, device=dev)
+        self._xn = torch.empty(p.t_local, dtype=torch.float32, device=dev)
+        self._vn = torch.empty(p.t_local, n_kv, dtype=torch.float32, device=dev)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._peers = []
+        self._open_peers()
+
+    def _open_peers(self):
+        """Peer pointer tables of every rank's K / V shard (CUDA IPC; own shard local)."""
+        mine = (self.ops.ipc_export(self.k_local), self.ops.ipc_export(self.v_local))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=self.group)
+        kp, vp = [], []
+        for r, ((kh, ko), (vh, vo)) in enumerate(allh):
+            if r == self.rank:
+                kp.append(self.k_local.data_ptr())
+                vp.append(self.v_local.data_ptr())
+            else:
+                kptr = self.ops.ipc_open(kh, ko)
+                vptr = self.ops.ipc_open(vh, vo)
+                self._peers += [(kptr, ko), (vptr, vo)]
+                kp.append(kptr)
+                vp.append(vptr)
+        dev = self.k_local.device
+        self.k_src = torch.tensor(kp, dtype=torch.int64, device=dev)
+        self.v_src = torch.tensor(vp, dtype=torch.int64, device=dev)
+
+    def close(self):
+        for ptr, off in self._peers:
+            self.ops.ipc_close(ptr, off)
+        self._peers = []
+
+    def forward(self, x, gate_weight, gate_bias, alpha, q):
+        """``x [T_local, d_model]`` and ``q [T_local, H, D]`` of this rank's positions (``k_local`` /
+        ``v_local`` already written). Returns this rank's attention output ``[T_local, H, D]``."""
+        ops, p = self.ops, self.plan
+        L = ops.L
+        # 1. own signals (value norms from the shard's values, as the single-GPU core)
+        L.call("dsalt_token_signals", ops._ptr(x), ops._dt(x), p.t_local, x.shape[1], x.stride(0),
+               ops._ptr(gate_weight), ops._ptr(gate_bias), ops._dt(gate_weight), self.n_min, self.n_max,
+               ops._ptr(self.v_local), ops._dt(self.v_local), self.v_local.stride(0), self.n_kv, self.head_dim,
+               L.NORM_F32, ops._ptr(self._w), ops._ptr(self._xn), ops._ptr(self._vn), None, ops._stream())
+        # 2. all ranks' signals
+        w, xn, vn = gather_signals(self._w, self._xn, self._vn, self.group)
+        # 3. landmark sets of the own blocks
+        lmk = ops.select_block_range(xn, vn, w, alpha, self.k_lmk, self.n_heads, self.block, p.set_lo, p.set_hi)
+        # 4. window halo from the previous rank
+        exchange_halo(self.k_ext, self.v_ext, p, self.halo_next, self.group)
+        # 5. attention of the own queries
+        ops.attention_sharded(q, self.k_ext, self.v_ext, p.q_pos0, p.kv_pos0, p.seq_len, w, lmk, self.block,
+                              self.k_src, self.v_src, p.t_local, out=self.out)
+        # 6. every rank is done reading the others' K / V
+        dist.all_reduce(self._flag, group=self.group)
+        return self.out, lmk

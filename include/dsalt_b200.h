@@ -117,6 +117,45 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
                         size_t workspace_bytes, void* stream);
 
 /*
+ * Sequence-sharded forms (no counterpart in the reference, which runs on one GPU): one
+ * rank's share of a single sequence of seq_len positions split across ranks.
+ *
+ * dsalt_select_block_range: the block-causal sets [set_lo, set_hi) of one sequence whose
+ *   signals (xnorm, vnorm, w: every position of the sequence, e.g. all-gathered from the
+ *   ranks) are given; only the prefix [0, set_hi * block) is read. Same sets as
+ *   dsalt_select_landmarks(DSALT_SELECT_BLOCK_CAUSAL) for those blocks. lmk_out
+ *   [n_heads, set_hi - set_lo, k].
+ * dsalt_attention_fwd_sharded: queries = positions [q_pos0, q_pos0 + q_rows) (q, out,
+ *   lse rows 0..q_rows-1); k/v rows = positions [kv_pos0, kv_pos0 + kv_rows), which must
+ *   hold every window key of the local queries (kv_pos0 <= q_pos0 - max width + 1; keys
+ *   below kv_pos0 read as zero); w [seq_len] widths by position; lmk [n_heads,
+ *   n_local_sets, k_lmk] positions within the sequence (one set per lmk_block local
+ *   queries, or one set when lmk_block = 0), ascending, -1 last. Landmark rows are read
+ *   from lmk_k_src[r] / lmk_v_src[r] (device arrays of pointers; rank r holds positions
+ *   [r * rows_per_src, (r+1) * rows_per_src) with the kv token stride), which may be other
+ *   GPUs' memory mapped by dsalt_ipc_open (plain NVLink loads). q_pos0 and q_rows are
+ *   multiples of 128 (and of lmk_block); bf16 / fp16 inputs; head_dim 64.
+ * dsalt_ipc_export / dsalt_ipc_open / dsalt_ipc_close: CUDA IPC handles (64 bytes) of a
+ *   device pointer inside an allocation, for the peer tables above.
+ */
+size_t dsalt_select_block_range_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block,
+                                                int set_hi);
+int dsalt_select_block_range(const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                             int64_t seq_len, int n_heads, int n_kv, int k, int block, int set_lo, int set_hi,
+                             int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream);
+size_t dsalt_attention_sharded_workspace_bytes(int64_t q_rows, int n_heads);
+int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int dtype, int64_t q_rows, int n_heads,
+                                int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, int64_t q_pos0,
+                                int64_t kv_pos0, int64_t kv_rows, int64_t seq_len, const int32_t* w,
+                                const int32_t* lmk, const float* lmk_bias, int k_lmk, int lmk_block,
+                                const void* const* lmk_k_src, const void* const* lmk_v_src, int64_t rows_per_src,
+                                void* out, int out_dtype, float* lse, void* workspace, size_t workspace_bytes,
+                                void* stream);
+int dsalt_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+int dsalt_ipc_open(const void* handle, int64_t offset, void** ptr_out);
+int dsalt_ipc_close(void* ptr, int64_t offset);
+
+/*
  * dsalt_attention_fwd without a workspace: no counterpart in the reference.
  * For callers that cannot allocate device memory: a host binding that holds only the
  * caller's q/k/v/out pointers and no device allocator of its own (a cgo, JNI or ctypes
