@@ -267,16 +267,16 @@ def run_sharded(args, rank, world, local, dev):
     w, xn, vn = None, None, None
     out, lmk = core.forward(xs, gw, gb, alpha, qs)
     from dsalt_b200.sharded import gather_signals
-    w, xn, vn = gather_signals(core._w, core._xn, core._vn, core.group)
+    w, xn, vn = gather_signals(core._w, core._xn, core._vn, core.group, out=core._sig)
     n_att = max(20, args.steps // 4)
     for _ in range(3):
         ops.attention_sharded(qs, core.k_ext, core.v_ext, p.q_pos0, p.kv_pos0, T, w, lmk, B, core.k_src, core.v_src,
-                              p.t_local, out=core.out)
+                              p.t_local, out=core.out, workspace=core._ws_att)
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(n_att):
         ops.attention_sharded(qs, core.k_ext, core.v_ext, p.q_pos0, p.kv_pos0, T, w, lmk, B, core.k_src, core.v_src,
-                              p.t_local, out=core.out)
+                              p.t_local, out=core.out, workspace=core._ws_att)
     e1.record(stream)
     torch.cuda.synchronize()
     att_ms = max_over_ranks(e0.elapsed_time(e1) / n_att, world)

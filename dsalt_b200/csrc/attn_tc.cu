@@ -71,12 +71,9 @@ struct Params {
   const int32_t* tile_base;
   const int4* plan;  // per query tile: {q row base, L, m0, set}, {kstart, nwt, kv row base, w base}
   // Sharded mode (shard_tiles > 0): the local query tiles cover positions q_pos0 + 128 t of
-  // one sequence; landmark rows come from the per-rank tables lmk_k_src / lmk_v_src (rank
-  // = position / rows_per_src, possibly another GPU's memory read over NVLink).
+  // one sequence; the landmark rows of each (local set, head) were gathered beforehand
+  // (lmk_gather_kernel) into tiles loaded by TMA like window tiles.
   int shard_tiles, n_sets_local;
-  const uint16_t* const* lmk_k_src;
-  const uint16_t* const* lmk_v_src;
-  int rows_per_src;
   float scale_log2;  // log2(e) / sqrt(head_dim)
   float inv_scale;   // sqrt(head_dim): landmark bias in raw-logit units
   uint32_t idesc_qk, idesc_pv;
@@ -263,7 +260,8 @@ __device__ __forceinline__ uint32_t pack_p(bool bf, float lo, float hi) {
 template <int HD, bool BF>
 __global__ void __launch_bounds__(NTHREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_lk,
+                       const __grid_constant__ CUtensorMap tm_lv, const Params p) {
   using SM = Smem<HD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -424,11 +422,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               for (int a = 0; a < SM::NA; ++a) tma_load_3d(vdst + a * BM * 128, &tm_v, &B.v_full[sv], a * 64, f.hk, row);
             }
           } else {
+            const int lt = -jt - 1;
+            if (p.shard_tiles > 0) {
+              // pre-gathered landmark tiles of (set, head)
+              const int row = ((f.set * p.H + f.h) * f.nlt + lt) * BN;
+              if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
+              if (lane == 0) {
+                mbar_arrive_expect_tx(&B.k_full[sk], SM::TILE_BYTES);
+                for (int a = 0; a < SM::NA; ++a) tma_load_3d(kdst + a * BM * 128, &tm_lk, &B.k_full[sk], a * 64, 0, row);
+              }
+              if (!mbar_wait(&B.v_empty[sv], ((uint32_t)(g / NSV) & 1) ^ 1, p.err, 14)) { ok = false; break; }
+              if (lane == 0) {
+                mbar_arrive_expect_tx(&B.v_full[sv], SM::TILE_BYTES);
+                for (int a = 0; a < SM::NA; ++a) tma_load_3d(vdst + a * BM * 128, &tm_lv, &B.v_full[sv], a * 64, 0, row);
+              }
+              continue;
+            }
             // landmark rows (replaces _build_landmark_kv): 16-byte cp.async by all lanes into
             // the swizzled tiles, four rows per instruction; empty slots are zero-filled
             // (their columns are masked by the row's landmark count, and zeros keep P·V
             // finite). The positions come from this item's slot.
-            const int lt = -jt - 1;
             if (!mbar_wait(&B.it_full[sl_i], (uint32_t)(it / NIS) & 1, p.err, 15)) { ok = false; break; }
             if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
             if (!mbar_wait(&B.v_empty[sv], ((uint32_t)(g / NSV) & 1) ^ 1, p.err, 14)) { ok = false; break; }
@@ -442,24 +455,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const int rr = j * RPI + rsub;
                 const int idx = lt * BN + rb + rr;
                 const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
-                const int pc = pos < 0 ? 0 : pos;
-                const uint16_t *ks, *vs;
-                int64_t row;
-                if (p.shard_tiles > 0) {
-                  const int src = pc / p.rows_per_src;
-                  ks = p.lmk_k_src[src];
-                  vs = p.lmk_v_src[src];
-                  row = pc - (int64_t)src * p.rows_per_src;
-                } else {
-                  ks = kg;
-                  vs = vg;
-                  row = (int64_t)f.kvb + pc;
-                }
-                const int64_t off = row * p.kv_stride + head_off;
+                const int64_t off = ((int64_t)f.kvb + (pos < 0 ? 0 : pos)) * p.kv_stride + head_off;
                 const uint32_t so = swz_off<HD>(rb + rr, c);
                 const uint32_t nb = pos < 0 ? 0u : 16u;
-                cp_async_16(kdst + so, ks + off, nb);
-                cp_async_16(vdst + so, vs + off, nb);
+                cp_async_16(kdst + so, kg + off, nb);
+                cp_async_16(vdst + so, vg + off, nb);
               }
             }
             cp_async_wait_all();
@@ -799,6 +799,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == 1) tmem_dealloc(tbase, TMEM_COLS);
 }
 
+// Sharded mode: the landmark K/V rows of every (local set, head) gathered into 128-row
+// tiles, [set][head][tile][row][D], rows past the set's length or with position -1 zero.
+// Rows are read from their owner rank's K/V shard (plain loads; peers' memory over NVLink).
+// One CTA per (set, head, tile), 16 bytes per thread and row chunk.
+template <int HD>
+__global__ void __launch_bounds__(256) lmk_gather_kernel(const int32_t* __restrict__ lmk, int H, int rep,
+                                                         int n_sets, int k, int nlt,
+                                                         const uint16_t* const* __restrict__ ksrc,
+                                                         const uint16_t* const* __restrict__ vsrc, int rows_per_src,
+                                                         int64_t kv_stride, uint16_t* __restrict__ lk,
+                                                         uint16_t* __restrict__ lv) {
+  constexpr int CPR = HD / 8;
+  const int lt = blockIdx.x % nlt, hs = blockIdx.x / nlt;  // hs = set * H + h
+  const int h = hs % H, set = hs / H, hk = h / rep;
+  const int32_t* P = lmk + ((int64_t)h * n_sets + set) * k;
+  uint16_t* dk = lk + (int64_t)blockIdx.x * BN * HD;
+  uint16_t* dv = lv + (int64_t)blockIdx.x * BN * HD;
+  for (int e = threadIdx.x; e < BN * CPR; e += blockDim.x) {
+    const int r = e / CPR, c = e - r * CPR;
+    const int idx = lt * BN + r;
+    const int pos = idx < k ? __ldg(P + idx) : -1;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = kv;
+    if (pos >= 0) {
+      const int src = pos / rows_per_src;
+      const int64_t off = (int64_t)(pos - src * rows_per_src) * kv_stride + (int64_t)hk * HD + c * 8;
+      kv = *reinterpret_cast<const uint4*>(ksrc[src] + off);
+      vv = *reinterpret_cast<const uint4*>(vsrc[src] + off);
+    }
+    reinterpret_cast<uint4*>(dk)[e] = kv;
+    reinterpret_cast<uint4*>(dv)[e] = vv;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -881,12 +914,21 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   p.set_base = set_base;
   p.tile_base = tile_base;
   p.plan = plan;
+  CUtensorMap mlk = mk, mlv = mv;
   if (shard) {
     p.shard_tiles = shard_tiles;
     p.n_sets_local = lmk_block ? (int)((shard->q_rows + lmk_block - 1) / lmk_block) : 1;
-    p.lmk_k_src = reinterpret_cast<const uint16_t* const*>(shard->lmk_k_src);
-    p.lmk_v_src = reinterpret_cast<const uint16_t* const*>(shard->lmk_v_src);
-    p.rows_per_src = (int)shard->rows_per_src;
+    const int nlt = (k_lmk + BN - 1) / BN;
+    const int64_t tiles = (int64_t)p.n_sets_local * H * nlt;
+    if (tiles > 0) {
+      lmk_gather_kernel<64><<<(unsigned)tiles, 256, 0, stream>>>(
+          lmk, H, H / Hkv, p.n_sets_local, k_lmk, nlt, reinterpret_cast<const uint16_t* const*>(shard->lmk_k_src),
+          reinterpret_cast<const uint16_t* const*>(shard->lmk_v_src), (int)shard->rows_per_src, kv_stride,
+          reinterpret_cast<uint16_t*>(shard->lmk_tiles_k), reinterpret_cast<uint16_t*>(shard->lmk_tiles_v));
+      if ((rc = check_cuda(cudaGetLastError(), "landmark gather launch"))) return rc;
+      if ((rc = make_map(&mlk, shard->lmk_tiles_k, dtype, HD, 1, tiles * BN, HD))) return rc;
+      if ((rc = make_map(&mlv, shard->lmk_tiles_v, dtype, HD, 1, tiles * BN, HD))) return rc;
+    }
   }
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
   p.inv_scale = (float)sqrt((double)HD);
@@ -909,7 +951,7 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "attention smem attr")))
     return rc;
-  kern<<<grid, NTHREADS, smem, stream>>>(mq, mk, mv, p);
+  kern<<<grid, NTHREADS, smem, stream>>>(mq, mk, mv, mlk, mlv, p);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 

@@ -210,10 +210,16 @@ int dsalt_select_block_range(const float* xnorm, const float* vnorm, const int32
                              workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
-size_t dsalt_attention_sharded_workspace_bytes(int64_t q_rows, int n_heads) {
-  (void)n_heads;
-  if (q_rows < 0) return 0;
-  return 256 + a256(32 * (size_t)(q_rows / 128 + 1));
+// plan | gathered landmark K tiles | V tiles
+static size_t sharded_tile_bytes(int64_t q_rows, int n_heads, int k_lmk, int lmk_block, int head_dim) {
+  const int64_t n_sets = lmk_block ? (q_rows + lmk_block - 1) / lmk_block : 1;
+  const int64_t nlt = (k_lmk + 127) / 128;
+  return a256((size_t)(n_sets * n_heads * nlt * 128) * head_dim * 2);
+}
+
+size_t dsalt_attention_sharded_workspace_bytes(int64_t q_rows, int n_heads, int k_lmk, int lmk_block, int head_dim) {
+  if (q_rows < 0 || n_heads < 1 || k_lmk < 0 || lmk_block < 0 || head_dim < 1) return 0;
+  return 256 + a256(32 * (size_t)(q_rows / 128 + 1)) + 2 * sharded_tile_bytes(q_rows, n_heads, k_lmk, lmk_block, head_dim);
 }
 
 int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int dtype, int64_t q_rows, int n_heads,
@@ -239,11 +245,15 @@ int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int
     return fail(DSALT_ERR_INVALID, "attention (sharded): token stride smaller than heads x head_dim");
   if (!q || !k || !v || !w || !out || (k_lmk > 0 && (!lmk || !lmk_k_src || !lmk_v_src)) || !workspace)
     return fail(DSALT_ERR_INVALID, "attention (sharded): null pointer");
-  const size_t need = dsalt_attention_sharded_workspace_bytes(q_rows, n_heads);
+  const size_t need = dsalt_attention_sharded_workspace_bytes(q_rows, n_heads, k_lmk, lmk_block, head_dim);
   if (workspace_bytes < need)
     return fail(DSALT_ERR_WORKSPACE, "attention (sharded): workspace %zu < %zu", workspace_bytes, need);
-  ShardArgs sa{q_pos0, q_rows, kv_pos0, kv_rows, seq_len, rows_per_src, lmk_k_src, lmk_v_src};
-  int4* plan = reinterpret_cast<int4*>(reinterpret_cast<char*>(workspace) + 256);
+  char* ws = reinterpret_cast<char*>(workspace);
+  const size_t plan_bytes = a256(32 * (size_t)(q_rows / 128 + 1));
+  const size_t tile_bytes = sharded_tile_bytes(q_rows, n_heads, k_lmk, lmk_block, head_dim);
+  ShardArgs sa{q_pos0, q_rows, kv_pos0, kv_rows, seq_len, rows_per_src, lmk_k_src, lmk_v_src,
+               ws + 256 + plan_bytes, ws + 256 + plan_bytes + tile_bytes};
+  int4* plan = reinterpret_cast<int4*>(ws + 256);
   int32_t* tables = reinterpret_cast<int32_t*>(workspace);
   return launch_attn_tc(q, k, v, dtype, q_rows, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
                         lmk_block, nullptr, 1, tables, tables + 32, plan, q_rows / 128, out, out_dtype, lse,

@@ -18,10 +18,13 @@ namespace dsalt {
 // q/out rows are positions [q_pos0, q_pos0 + q_rows) of one sequence of seq_len positions,
 // k/v rows are positions [kv_pos0, kv_pos0 + kv_rows); landmark row of position p is row
 // p - r * rows_per_src of rank r = p / rows_per_src's K/V (device arrays of pointers).
+// lmk_tiles_k / lmk_tiles_v: workspace for the gathered landmark tiles of the local sets.
 struct ShardArgs {
   int64_t q_pos0, q_rows, kv_pos0, kv_rows, seq_len, rows_per_src;
   const void* const* lmk_k_src;
   const void* const* lmk_v_src;
+  void* lmk_tiles_k;
+  void* lmk_tiles_v;
 };
 
 // --------------------------------------------------------------------------

@@ -30,6 +30,7 @@ namespace dsalt {
 
 constexpr int NBIN = 32;                 // bins per signal for the dominance grid
 constexpr int NCELL = NBIN * NBIN;
+static_assert(NBIN == 32, "the dominance grid scans assume one bin per lane");
 constexpr int GCHUNK = 4096;             // positions per CTA in whole-sequence phase 1
 constexpr int STAT_CHUNK = 512;          // tokens per partial sum in whole-sequence mode
 constexpr int SEL_THREADS = 512;
@@ -122,11 +123,17 @@ __device__ __forceinline__ DD block_dd_sum(DD v, DD* red) {
   return r;  // valid in thread 0
 }
 
-__global__ void chunk_sums_kernel(const float* __restrict__ xn, const float* __restrict__ vn, int n_kv,
-                                  const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
-                                  Partial* __restrict__ part) {
-  __shared__ DD red1[32], red2[32];
-  const int c = blockIdx.x, sig = blockIdx.y, nsig = 1 + n_kv;
+// one warp per (chunk, signal): the double-double reduction is the costly part (fp64
+// bound), so it runs once per warp rather than across a whole block
+__global__ void __launch_bounds__(256) chunk_sums_kernel(const float* __restrict__ xn, const float* __restrict__ vn,
+                                                         int n_kv, const int32_t* __restrict__ cu, int n_seqs,
+                                                         const int32_t* __restrict__ base, int C, int n_chunks,
+                                                         Partial* __restrict__ part) {
+  const int nsig = 1 + n_kv;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid >= (int64_t)n_chunks * nsig) return;
+  const int c = (int)(wid / nsig), sig = (int)(wid % nsig);
   const int total = base[n_seqs];
   Partial out{0.0, 0.0, 0.0, 0.0};
   if (c < total) {
@@ -135,16 +142,16 @@ __global__ void chunk_sums_kernel(const float* __restrict__ xn, const float* __r
     const int a = cu[s] + lc * C;
     const int b = min(cu[s + 1], a + C);
     DD s1{0.0, 0.0}, s2{0.0, 0.0};
-    for (int t = a + threadIdx.x; t < b; t += blockDim.x) {
+    for (int t = a + lane; t < b; t += 32) {
       const double v = (double)(sig == 0 ? xn[t] : vn[(int64_t)t * n_kv + sig - 1]);
       s1 = dd_add_d(s1, v);
       s2 = dd_add_d(s2, __dmul_rn(v, v));  // exact: the square of an fp32 value fits a double
     }
-    DD r1 = block_dd_sum(s1, red1);
-    DD r2 = block_dd_sum(s2, red2);
-    out = Partial{r1.hi, r1.lo, r2.hi, r2.lo};
+    s1 = dd_warp_sum(s1);
+    s2 = dd_warp_sum(s2);
+    out = Partial{s1.hi, s1.lo, s2.hi, s2.lo};
   }
-  if (threadIdx.x == 0) part[(int64_t)c * nsig + sig] = out;
+  if (lane == 0) part[(int64_t)c * nsig + sig] = out;
 }
 
 // ---------------------------------------------------------------------------
@@ -511,20 +518,26 @@ __global__ void __launch_bounds__(256) dominance_hist_kernel(
     if (p >= w[t]) atomicAdd(&hist[bin_of(vn[t * n_kv + g], ev) * NBIN + bin_of(xn[t], ex)], 1);
   }
   __syncthreads();
-  if (threadIdx.x < NBIN) {  // suffix along x bins
-    int run = 0;
-    for (int b = NBIN - 1; b >= 0; --b) {
-      run += hist[threadIdx.x * NBIN + b];
-      hist[threadIdx.x * NBIN + b] = run;
+  // 2-D suffix sums, one warp-wide scan per row then per column (lane = bin)
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int row = wid; row < NBIN; row += nw) {  // along x bins
+    int v = hist[row * NBIN + lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += y;
     }
+    hist[row * NBIN + lane] = v;
   }
   __syncthreads();
-  if (threadIdx.x < NBIN) {  // suffix along value bins
-    int run = 0;
-    for (int a = NBIN - 1; a >= 0; --a) {
-      run += hist[a * NBIN + threadIdx.x];
-      hist[a * NBIN + threadIdx.x] = run;
+  for (int col = wid; col < NBIN; col += nw) {  // along value bins
+    int v = hist[lane * NBIN + col];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += y;
     }
+    hist[lane * NBIN + col] = v;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < NCELL; i += blockDim.x) out[i] = hist[i];
@@ -844,7 +857,9 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
   const int C = mode == DSALT_SELECT_GLOBAL ? STAT_CHUNK : block;
   const int nsig = L.nsig;
   chunk_table_kernel<<<1, 1024, 0, stream>>>(cu, n_seqs, C, cbase);
-  chunk_sums_kernel<<<dim3(L.max_chunks, nsig), 256, 0, stream>>>(xnorm, vnorm, n_kv, cu, n_seqs, cbase, C, part);
+  chunk_sums_kernel<<<(unsigned)(((int64_t)L.max_chunks * nsig + 7) / 8), 256, 0, stream>>>(xnorm, vnorm, n_kv, cu,
+                                                                                           n_seqs, cbase, C,
+                                                                                           L.max_chunks, part);
   if (mode == DSALT_SELECT_GLOBAL) {
     float* gstats = reinterpret_cast<float*>(ws + L.gstats_off);
     int32_t* gbase = reinterpret_cast<int32_t*>(ws + L.gbase_off);

@@ -311,7 +311,7 @@ def attention_sharded(q, k, v, q_pos0: int, kv_pos0: int, seq_len: int, w, lmk, 
         raise ValueError("q, k, v must have contiguous heads and k, v the same token stride")
     if out is None:
         out = torch.empty(q_rows, H, D, dtype=q.dtype, device=q.device)
-    n = L.query("dsalt_attention_sharded_workspace_bytes", q_rows, H)
+    n = L.query("dsalt_attention_sharded_workspace_bytes", q_rows, H, int(lmk.shape[-1]), int(lmk_block), D)
     ws = workspace if workspace is not None and workspace.numel() >= n else _workspace(n, q.device)
     bias = None if lmk_bias is None else lmk_bias.float().contiguous()
     L.call("dsalt_attention_fwd_sharded", _ptr(q), _ptr(k), _ptr(v), _dt(q), q_rows, H, n_kv, D, q.stride(0),

@@ -72,24 +72,30 @@ def shard_plan(seq_len: int, world: int, rank: int, n_max: int, block: int = 512
     return ShardPlan(world, rank, seq_len, t_local, q_pos0, halo, block)
 
 
-def gather_signals(w_loc: torch.Tensor, xn_loc: torch.Tensor, vn_loc: torch.Tensor, group=None):
-    """All-gather the per-token signals of every rank's shard (one collective).
+def gather_signals(w_loc: torch.Tensor, xn_loc: torch.Tensor, vn_loc: torch.Tensor, group=None, out=None):
+    """All-gather the per-token signals of every rank's shard.
 
     ``w_loc [T]`` int32, ``xn_loc [T]`` fp32, ``vn_loc [T, H_kv]`` fp32 →
-    ``(w [P·T], xn [P·T], vn [P·T, H_kv])`` in position order."""
+    ``(w [P·T], xn [P·T], vn [P·T, H_kv])`` in position order, gathered straight into the
+    output tensors (``out``, reused across steps when given); over NCCL the three
+    collectives are issued as one group."""
     T = w_loc.shape[0]
     n_kv = vn_loc.shape[1]
-    flat = torch.empty(T * (2 + n_kv), dtype=torch.int32, device=w_loc.device)
-    flat[:T] = w_loc
-    flat[T:2 * T] = xn_loc.view(torch.int32)
-    flat[2 * T:] = vn_loc.reshape(-1).view(torch.int32)
     P = dist.get_world_size(group)
-    out = torch.empty(P * flat.numel(), dtype=torch.int32, device=flat.device)
-    dist.all_gather_into_tensor(out, flat, group=group)
-    out = out.view(P, flat.numel())
-    w = out[:, :T].reshape(P * T)
-    xn = out[:, T:2 * T].reshape(P * T).view(torch.float32)
-    vn = out[:, 2 * T:].reshape(P * T, n_kv).view(torch.float32)
+    if out is None:
+        out = (torch.empty(P * T, dtype=torch.int32, device=w_loc.device),
+               torch.empty(P * T, dtype=torch.float32, device=w_loc.device),
+               torch.empty(P * T, n_kv, dtype=torch.float32, device=w_loc.device))
+    w, xn, vn = out
+    pairs = ((w, w_loc), (xn, xn_loc), (vn.view(-1), vn_loc.reshape(-1)))
+    if dist.get_backend(group) == "nccl":
+        with dist._coalescing_manager(group, w_loc.device, async_ops=True) as cm:
+            for o, i in pairs:
+                dist.all_gather_into_tensor(o, i, group=group)
+        cm.wait()
+    else:
+        for o, i in pairs:
+            dist.all_gather_into_tensor(o, i, group=group)
     return w, xn, vn
 
 
@@ -138,6 +144,14 @@ class ShardedCore:
         self._xn = torch.empty(p.t_local, dtype=torch.float32, device=dev)
         self._vn = torch.empty(p.t_local, n_kv, dtype=torch.float32, device=dev)
         self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        L = seq_len
+        self._sig = (torch.empty(L, dtype=torch.int32, device=dev), torch.empty(L, dtype=torch.float32, device=dev),
+                     torch.empty(L, n_kv, dtype=torch.float32, device=dev))
+        L_ = ops.L
+        nsel = L_.query("dsalt_select_block_range_workspace_bytes", seq_len, n_heads, n_kv, k_lmk, block, p.set_hi)
+        natt = L_.query("dsalt_attention_sharded_workspace_bytes", p.t_local, n_heads, k_lmk, block, head_dim)
+        self._ws_sel = torch.empty(max(nsel, 1), dtype=torch.uint8, device=dev)
+        self._ws_att = torch.empty(max(natt, 1), dtype=torch.uint8, device=dev)
         self._peers = []
         self._open_peers()
 
@@ -177,14 +191,15 @@ class ShardedCore:
                ops._ptr(self.v_local), ops._dt(self.v_local), self.v_local.stride(0), self.n_kv, self.head_dim,
                L.NORM_F32, ops._ptr(self._w), ops._ptr(self._xn), ops._ptr(self._vn), None, ops._stream())
         # 2. all ranks' signals
-        w, xn, vn = gather_signals(self._w, self._xn, self._vn, self.group)
+        w, xn, vn = gather_signals(self._w, self._xn, self._vn, self.group, out=self._sig)
         # 3. landmark sets of the own blocks
-        lmk = ops.select_block_range(xn, vn, w, alpha, self.k_lmk, self.n_heads, self.block, p.set_lo, p.set_hi)
+        lmk = ops.select_block_range(xn, vn, w, alpha, self.k_lmk, self.n_heads, self.block, p.set_lo, p.set_hi,
+                                     workspace=self._ws_sel)
         # 4. window halo from the previous rank
         exchange_halo(self.k_ext, self.v_ext, p, self.halo_next, self.group)
         # 5. attention of the own queries
         ops.attention_sharded(q, self.k_ext, self.v_ext, p.q_pos0, p.kv_pos0, p.seq_len, w, lmk, self.block,
-                              self.k_src, self.v_src, p.t_local, out=self.out)
+                              self.k_src, self.v_src, p.t_local, out=self.out, workspace=self._ws_att)
         # 6. every rank is done reading the others' K / V
         dist.all_reduce(self._flag, group=self.group)
         return self.out, lmk

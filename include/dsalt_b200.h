@@ -133,8 +133,9 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
  *   queries, or one set when lmk_block = 0), ascending, -1 last. Landmark rows are read
  *   from lmk_k_src[r] / lmk_v_src[r] (device arrays of pointers; rank r holds positions
  *   [r * rows_per_src, (r+1) * rows_per_src) with the kv token stride), which may be other
- *   GPUs' memory mapped by dsalt_ipc_open (plain NVLink loads). q_pos0 and q_rows are
- *   multiples of 128 (and of lmk_block); bf16 / fp16 inputs; head_dim 64.
+ *   GPUs' memory mapped by dsalt_ipc_open (plain NVLink loads), gathered once per call into
+ *   the workspace as 128-row tiles. q_pos0 and q_rows are multiples of 128 (and of
+ *   lmk_block); bf16 / fp16 inputs; head_dim 64.
  * dsalt_ipc_export / dsalt_ipc_open / dsalt_ipc_close: CUDA IPC handles (64 bytes) of a
  *   device pointer inside an allocation, for the peer tables above.
  */
@@ -143,7 +144,7 @@ size_t dsalt_select_block_range_workspace_bytes(int64_t seq_len, int n_heads, in
 int dsalt_select_block_range(const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
                              int64_t seq_len, int n_heads, int n_kv, int k, int block, int set_lo, int set_hi,
                              int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream);
-size_t dsalt_attention_sharded_workspace_bytes(int64_t q_rows, int n_heads);
+size_t dsalt_attention_sharded_workspace_bytes(int64_t q_rows, int n_heads, int k_lmk, int lmk_block, int head_dim);
 int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int dtype, int64_t q_rows, int n_heads,
                                 int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, int64_t q_pos0,
                                 int64_t kv_pos0, int64_t kv_rows, int64_t seq_len, const int32_t* w,
