@@ -35,6 +35,8 @@ constexpr int GCHUNK = 4096;             // positions per CTA in whole-sequence 
 constexpr int STAT_CHUNK = 512;          // tokens per partial sum in whole-sequence mode
 constexpr int SEL_THREADS = 512;
 constexpr int KEY_CAP = 8192;            // candidate keys cached in shared memory
+constexpr int BSEL_THREADS = 256;        // block-causal select: small CTAs, several per SM
+constexpr int BSEL_KEY_CAP = 2048;       // its key cache (the prefix-dominance filter keeps ~1K)
 constexpr int MAX_K = 1024;
 
 // thresholds (in units of the sequence's std above its mean) of the dominance grid:
@@ -513,9 +515,17 @@ __global__ void __launch_bounds__(256) dominance_hist_kernel(
   const int start = cu[s];
   const int p0 = (c - base[s]) * C;
   const int p1 = min(cu[s + 1] - start, p0 + C);
-  for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
-    const int64_t t = start + p;
-    if (p >= w[t]) atomicAdd(&hist[bin_of(vn[t * n_kv + g], ev) * NBIN + bin_of(xn[t], ex)], 1);
+  // tokens of a chunk cluster in few cells: one shared-memory atomic per distinct cell
+  // and warp
+  for (int p0w = p0; p0w < p1; p0w += blockDim.x) {
+    const int p = p0w + threadIdx.x;
+    int cell = -1;
+    if (p < p1) {
+      const int64_t t = start + p;
+      if (p >= w[t]) cell = bin_of(vn[t * n_kv + g], ev) * NBIN + bin_of(xn[t], ex);
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, cell);
+    if (cell >= 0 && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[cell], __popc(same));
   }
   __syncthreads();
   // 2-D suffix sums, one warp-wide scan per row then per column (lane = bin)
@@ -541,6 +551,69 @@ __global__ void __launch_bounds__(256) dominance_hist_kernel(
   }
   __syncthreads();
   for (int i = threadIdx.x; i < NCELL; i += blockDim.x) out[i] = hist[i];
+}
+
+// The same grids for all kv groups of a chunk in one 512-thread CTA (n_kv <= 32): the
+// token loads, ‖x‖ bins and coverage tests are shared by the groups, and one CTA per chunk
+// amortises the latency of the scans. Shared memory: n_kv 32×32 grids + edges.
+__global__ void __launch_bounds__(512) dominance_hist_all_kernel(
+    const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w, int n_kv,
+    const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
+    const float* __restrict__ edges, int32_t* __restrict__ G) {
+  // grids with rows padded to NBIN+1 entries, so that column scans hit distinct banks
+  constexpr int RS = NBIN + 1;
+  extern __shared__ int32_t hs[];
+  int32_t* hist = hs;                                            // [n_kv][NBIN][RS]
+  float* ev = reinterpret_cast<float*>(hs + n_kv * NBIN * RS);   // [n_kv][NBIN-1]
+  __shared__ float ex[NBIN - 1];
+  const int c = blockIdx.x, nsig = 1 + n_kv;
+  const int total = base[n_seqs];
+  if (c >= total) return;
+  const int s = find_seq(base, n_seqs, c);
+  for (int i = threadIdx.x; i < n_kv * NBIN * RS; i += blockDim.x) hist[i] = 0;
+  if (threadIdx.x < NBIN - 1) ex[threadIdx.x] = edges[((int64_t)s * nsig + 0) * (NBIN - 1) + threadIdx.x];
+  for (int i = threadIdx.x; i < n_kv * (NBIN - 1); i += blockDim.x)
+    ev[i] = edges[((int64_t)s * nsig + 1) * (NBIN - 1) + i];  // groups 1..n_kv are consecutive
+  __syncthreads();
+  const int start = cu[s];
+  const int p0 = (c - base[s]) * C;
+  const int p1 = min(cu[s + 1] - start, p0 + C);
+  for (int p0w = p0; p0w < p1; p0w += blockDim.x) {
+    const int p = p0w + threadIdx.x;
+    const int64_t t = start + p;
+    const bool live = p < p1 && p >= w[t];
+    const int bx = live ? bin_of(xn[t], ex) : 0;
+    for (int g = 0; g < n_kv; ++g) {
+      const int cell = live ? (g * NBIN + bin_of(vn[t * n_kv + g], ev + g * (NBIN - 1))) * RS + bx : -1;
+      const unsigned same = __match_any_sync(0xffffffffu, cell);
+      if (cell >= 0 && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[cell], __popc(same));
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int row = wid; row < n_kv * NBIN; row += nw) {  // suffix along x bins, row = (g, value bin)
+    int v = hist[row * RS + lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += y;
+    }
+    hist[row * RS + lane] = v;
+  }
+  __syncthreads();
+  for (int col = wid; col < n_kv * NBIN; col += nw) {  // suffix along value bins, col = (g, x bin)
+    const int g = col / NBIN, b = col % NBIN;
+    int v = hist[(g * NBIN + lane) * RS + b];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_down_sync(0xffffffffu, v, o);
+      if (lane + o < 32) v += y;
+    }
+    hist[(g * NBIN + lane) * RS + b] = v;
+  }
+  __syncthreads();
+  int32_t* out = G + (int64_t)c * n_kv * NCELL;
+  for (int i = threadIdx.x; i < n_kv * NCELL; i += blockDim.x) out[i] = hist[(i / NBIN) * RS + (i % NBIN)];
 }
 
 // exclusive prefix over the chunks of each sequence, in place: G[c] <- Σ_{c'<c} G[c']
@@ -623,8 +696,60 @@ __global__ void survivor_kernel(const float* __restrict__ xn, const float* __res
   if (threadIdx.x == 0) surv_cnt[(int64_t)c * n_kv + g] = carry;
 }
 
+// survivor_kernel for all kv groups of a chunk in one 512-thread CTA (n_kv <= 32); the
+// records of a (chunk, group) are compacted in no particular order (the selection does not
+// depend on it)
+__global__ void __launch_bounds__(512) survivor_all_kernel(
+    const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w, int n_kv,
+    const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
+    const float* __restrict__ edges, const int32_t* __restrict__ D, int k, int32_t* __restrict__ surv_cnt,
+    int4* __restrict__ surv_rec) {
+  extern __shared__ float es[];  // [n_kv][NBIN-1]
+  __shared__ float ex[NBIN - 1];
+  __shared__ int32_t cnt[32];
+  const int c = blockIdx.x, nsig = 1 + n_kv;
+  const int total = base[n_seqs];
+  if (c >= total) return;
+  const int s = find_seq(base, n_seqs, c);
+  if (threadIdx.x < NBIN - 1) ex[threadIdx.x] = edges[((int64_t)s * nsig + 0) * (NBIN - 1) + threadIdx.x];
+  for (int i = threadIdx.x; i < n_kv * (NBIN - 1); i += blockDim.x)
+    es[i] = edges[((int64_t)s * nsig + 1) * (NBIN - 1) + i];
+  if (threadIdx.x < 32) cnt[threadIdx.x] = 0;
+  __syncthreads();
+  const int start = cu[s];
+  const int p0 = (c - base[s]) * C;
+  const int p1 = min(cu[s + 1] - start, p0 + C);
+  const int lane = threadIdx.x & 31;
+  for (int p0w = p0; p0w < p1; p0w += blockDim.x) {
+    const int p = p0w + threadIdx.x;
+    const int64_t t = start + p;
+    const bool live = p < p1 && p >= w[t];
+    const float xv = live ? xn[t] : 0.0f;
+    const int bx = live ? bin_of(xv, ex) : 0;
+    for (int g = 0; g < n_kv; ++g) {
+      bool keep = false;
+      int4 rec;
+      if (live) {
+        const float vv = vn[t * n_kv + g];
+        const int a = bin_of(vv, es + g * (NBIN - 1));
+        const int cell = (a == NBIN - 1 || bx == NBIN - 1) ? -1 : (a + 1) * NBIN + (bx + 1);
+        const int dom = cell < 0 ? 0 : D[((int64_t)c * n_kv + g) * NCELL + cell];
+        keep = dom < k;
+        rec = make_int4(p, __float_as_int(xv), __float_as_int(vv), cell);
+      }
+      const unsigned ball = __ballot_sync(0xffffffffu, keep);
+      int slot0 = 0;
+      if (lane == 0 && ball) slot0 = atomicAdd(&cnt[g], __popc(ball));
+      slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+      if (keep) surv_rec[((int64_t)c * n_kv + g) * C + slot0 + __popc(ball & ((1u << lane) - 1))] = rec;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < n_kv) surv_cnt[(int64_t)c * n_kv + threadIdx.x] = cnt[threadIdx.x];
+}
+
 // per (block set, head): exact scores of the surviving candidates of earlier chunks
-__global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
+__global__ void __launch_bounds__(BSEL_THREADS) block_select_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w,
     const float* __restrict__ alpha, const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base,
     int C, int n_heads, int n_kv, int k, const double2* __restrict__ stats, const int32_t* __restrict__ D,
@@ -667,7 +792,7 @@ __global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
   };
   if (!pruned) {
     // every uncovered position of the prefix is a candidate
-    if (n <= KEY_CAP) {
+    if (n <= BSEL_KEY_CAP) {
       for (int i = threadIdx.x; i < n; i += blockDim.x) keys[i] = score_key(i);
       __syncthreads();
       block_topk_positions([&](int i) { return keys[i]; }, n, k, sm, sel, out);
@@ -745,12 +870,12 @@ __global__ void __launch_bounds__(SEL_THREADS) block_select_kernel(
       if (lane == 0 && ball) slot0 = atomicAdd(&ncand, __popc(ball));
       slot0 = __shfl_sync(0xffffffffu, slot0, 0);
       const int slot = slot0 + __popc(ball & ((1u << lane) - 1));
-      if (key != 0 && slot < KEY_CAP) keys[slot] = key;
+      if (key != 0 && slot < BSEL_KEY_CAP) keys[slot] = key;
     }
   }
   __syncthreads();
   const int N = ncand;
-  if (N <= KEY_CAP) {
+  if (N <= BSEL_KEY_CAP) {
     block_topk_positions([&](int i) { return keys[i]; }, N, k, sm, sel, out);
   } else {
     // more candidates than the cache holds: evaluate them from the survivor lists
@@ -881,14 +1006,25 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
     int32_t* cnt = reinterpret_cast<int32_t*>(ws + L.cnt_off);
     int4* recs = reinterpret_cast<int4*>(ws + L.pos_off);
     block_stats_kernel<<<dim3(n_seqs, nsig), 256, 0, stream>>>(part, cu, n_seqs, cbase, nsig, C, stats, edges);
-    dominance_hist_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
-                                                                        edges, G);
+    if (n_kv <= 32) {
+      const size_t smh = (size_t)n_kv * (NBIN * (NBIN + 1) * sizeof(int32_t) + (NBIN - 1) * sizeof(float));
+      dominance_hist_all_kernel<<<L.max_chunks, 512, smh, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
+                                                                     edges, G);
+    } else {
+      dominance_hist_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase,
+                                                                          C, edges, G);
+    }
     dominance_scan_kernel<<<dim3(n_seqs * n_kv, NCELL / 256), 256, 0, stream>>>(G, cbase, n_kv);
-    survivor_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges,
-                                                                  G, k, cnt, recs);
-    const size_t sm3 = sizeof(uint64_t) * KEY_CAP;
+    if (n_kv <= 32) {
+      survivor_all_kernel<<<L.max_chunks, 512, (size_t)n_kv * (NBIN - 1) * sizeof(float), stream>>>(
+          xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges, G, k, cnt, recs);
+    } else {
+      survivor_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
+                                                                    edges, G, k, cnt, recs);
+    }
+    const size_t sm3 = sizeof(uint64_t) * BSEL_KEY_CAP;
     const bool range = set_hi >= 0;
-    block_select_kernel<<<dim3(range ? set_hi - set_lo : L.max_chunks, n_heads), SEL_THREADS, sm3, stream>>>(
+    block_select_kernel<<<dim3(range ? set_hi - set_lo : L.max_chunks, n_heads), BSEL_THREADS, sm3, stream>>>(
         xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, G, cnt, recs, lmk_out,
         range ? set_lo : 0, range ? set_hi - set_lo : 0);
   }
@@ -936,8 +1072,12 @@ int select_set_up_attributes() {
                                            (int)(sizeof(uint64_t) * KEY_CAP)),
                       "smem attr");
   if (rc) return rc;
+  rc = check_cuda(cudaFuncSetAttribute(dominance_hist_all_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)(32 * (NBIN * (NBIN + 1) * sizeof(int32_t) + (NBIN - 1) * sizeof(float)))),
+                  "smem attr");
+  if (rc) return rc;
   return check_cuda(cudaFuncSetAttribute(block_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(sizeof(uint64_t) * KEY_CAP)),
+                                         (int)(sizeof(uint64_t) * BSEL_KEY_CAP)),
                     "smem attr");
 }
 
