@@ -37,6 +37,7 @@ constexpr int SEL_THREADS = 512;
 constexpr int KEY_CAP = 8192;            // candidate keys cached in shared memory
 constexpr int BSEL_THREADS = 256;        // block-causal select: small CTAs, several per SM
 constexpr int BSEL_KEY_CAP = 2048;       // its key cache (the prefix-dominance filter keeps ~1K)
+constexpr int BSEL_REC_CAP = 8192;       // survivors whose chunk index is tabulated
 constexpr int MAX_K = 1024;
 
 // thresholds (in units of the sequence's std above its mean) of the dominance grid:
@@ -486,10 +487,12 @@ __global__ void block_stats_kernel(const Partial* __restrict__ part, const int32
   }
 }
 
+// number of the NBIN-1 ascending thresholds e[j] <= v (binary search)
 __device__ __forceinline__ int bin_of(float v, const float* e) {
   int b = 0;
 #pragma unroll
-  for (int j = 0; j < NBIN - 1; ++j) b += (e[j] <= v) ? 1 : 0;
+  for (int step = NBIN / 2; step > 0; step >>= 1)
+    if (b + step - 1 < NBIN - 1 && e[b + step - 1] <= v) b += step;
   return b;
 }
 
@@ -616,15 +619,20 @@ __global__ void __launch_bounds__(512) dominance_hist_all_kernel(
   for (int i = threadIdx.x; i < n_kv * NCELL; i += blockDim.x) out[i] = hist[(i / NBIN) * RS + (i % NBIN)];
 }
 
-// exclusive prefix over the chunks of each sequence, in place: G[c] <- Σ_{c'<c} G[c']
-__global__ void dominance_scan_kernel(int32_t* __restrict__ G, const int32_t* __restrict__ base, int n_kv) {
+// exclusive prefix over the chunks of each sequence, in place: G[c] <- Σ_{c'<c} G[c'].
+// Two passes over segments of SCAN_SEG chunks: segment totals, then each segment's scan
+// started from the sum of the totals before it (more independent chains in flight).
+constexpr int SCAN_SEG = 16;
+constexpr int SEG_SCAN_MAX_SEQS = 16;  // segment totals are kept per sequence
+
+// single pass (packed inputs with many sequences): one thread per (sequence, group, cell)
+__global__ void dominance_scan_serial_kernel(int32_t* __restrict__ G, const int32_t* __restrict__ base, int n_kv) {
   const int s = blockIdx.x / n_kv, g = blockIdx.x % n_kv;
   const int cell = blockIdx.y * blockDim.x + threadIdx.x;
   if (cell >= NCELL) return;
   int run = 0;
   const int c_end = base[s + 1];
   const int64_t stride = (int64_t)n_kv * NCELL;
-  // batches of 16 chunks: all loads of a batch are in flight before its stores
   for (int c0 = base[s]; c0 < c_end; c0 += 16) {
     int32_t* p = G + ((int64_t)c0 * n_kv + g) * NCELL + cell;
     int v[16];
@@ -635,6 +643,46 @@ __global__ void dominance_scan_kernel(int32_t* __restrict__ G, const int32_t* __
       if (c0 + j < c_end) p[j * stride] = run;
       run += v[j];
     }
+  }
+}
+
+__global__ void dominance_segsum_kernel(const int32_t* __restrict__ G, const int32_t* __restrict__ base, int n_seqs,
+                                        int n_kv, int max_segs, int32_t* __restrict__ segsum) {
+  const int s = blockIdx.x / n_kv, g = blockIdx.x % n_kv;
+  const int cell = threadIdx.x + blockIdx.z * blockDim.x;
+  const int seg = blockIdx.y;
+  const int c0 = base[s] + seg * SCAN_SEG, c_end = base[s + 1];
+  if (cell >= NCELL) return;
+  int v = 0;
+  if (c0 < c_end) {
+    const int64_t stride = (int64_t)n_kv * NCELL;
+    const int32_t* p = G + ((int64_t)c0 * n_kv + g) * NCELL + cell;
+#pragma unroll
+    for (int j = 0; j < SCAN_SEG; ++j) v += c0 + j < c_end ? p[j * stride] : 0;
+  }
+  segsum[(((int64_t)s * n_kv + g) * max_segs + seg) * NCELL + cell] = v;
+}
+
+__global__ void dominance_scan_kernel(int32_t* __restrict__ G, const int32_t* __restrict__ base, int n_kv,
+                                      int max_segs, const int32_t* __restrict__ segsum) {
+  const int s = blockIdx.x / n_kv, g = blockIdx.x % n_kv;
+  const int cell = threadIdx.x + blockIdx.z * blockDim.x;
+  const int seg = blockIdx.y;
+  if (cell >= NCELL) return;
+  const int c0 = base[s] + seg * SCAN_SEG, c_end = base[s + 1];
+  if (c0 >= c_end) return;
+  int run = 0;
+  const int32_t* ss = segsum + ((int64_t)s * n_kv + g) * max_segs * NCELL + cell;
+  for (int q = 0; q < seg; ++q) run += ss[(int64_t)q * NCELL];
+  const int64_t stride = (int64_t)n_kv * NCELL;
+  int32_t* p = G + ((int64_t)c0 * n_kv + g) * NCELL + cell;
+  int v[SCAN_SEG];
+#pragma unroll
+  for (int j = 0; j < SCAN_SEG; ++j) v[j] = c0 + j < c_end ? p[j * stride] : 0;
+#pragma unroll
+  for (int j = 0; j < SCAN_SEG; ++j) {
+    if (c0 + j < c_end) p[j * stride] = run;
+    run += v[j];
   }
 }
 
@@ -763,6 +811,7 @@ __global__ void __launch_bounds__(BSEL_THREADS) block_select_kernel(
   __shared__ int32_t wsum[32];
   __shared__ int32_t dsm[NCELL];
   __shared__ int32_t ncand;
+  __shared__ uint16_t chunk_of[BSEL_REC_CAP];  // survivor index -> chunk (when they fit)
   // sets set_lo + blockIdx.x; output [H, n_out, k] (n_out = all sets, or the range's)
   const int c = set_lo + blockIdx.x, h = blockIdx.y;
   const int total = base[n_seqs];
@@ -843,16 +892,27 @@ __global__ void __launch_bounds__(BSEL_THREADS) block_select_kernel(
     return make_key(sc, r.x);
   };
   // survivor i of the prefix lies in chunk j with offs[j] <= i < offs[j+1]
+  const int NS = offs[b];
+  const bool tab = NS <= BSEL_REC_CAP;
+  if (tab) {
+    for (int j = wid; j < b; j += (int)(blockDim.x >> 5))
+      for (int i = offs[j] + lane; i < offs[j + 1]; i += 32) chunk_of[i] = (uint16_t)j;
+    __syncthreads();
+  }
   auto rec_of = [&](int i) -> const int4* {
-    int lo = 0, hi = b;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (offs[mid] <= i) lo = mid;
-      else hi = mid;
+    int lo = 0;
+    if (tab) {
+      lo = chunk_of[i];
+    } else {
+      int hi = b;
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (offs[mid] <= i) lo = mid;
+        else hi = mid;
+      }
     }
     return surv_rec + ((int64_t)(c0 + lo) * n_kv + g) * C + (i - offs[lo]);
   };
-  const int NS = offs[b];
   constexpr int U = 4;  // records per thread in flight
   for (int i0 = threadIdx.x; i0 - (int)threadIdx.x < NS; i0 += U * blockDim.x) {
     int4 r[U];
@@ -893,8 +953,9 @@ __global__ void __launch_bounds__(BSEL_THREADS) block_select_kernel(
 static inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 struct SelectLayout {
-  size_t base_off, part_off, gstats_off, gbase_off, cand_off, stats_off, edges_off, G_off, cnt_off, pos_off, total;
-  int max_chunks, max_gchunks, nsig;
+  size_t base_off, part_off, gstats_off, gbase_off, cand_off, stats_off, edges_off, G_off, seg_off, cnt_off, pos_off,
+      total;
+  int max_chunks, max_gchunks, nsig, max_segs;
 };
 
 static SelectLayout select_layout(int mode, int64_t T, int n_seqs, int n_heads, int n_kv, int k, int block) {
@@ -922,6 +983,9 @@ static SelectLayout select_layout(int mode, int64_t T, int n_seqs, int n_heads, 
     off = align256(off + sizeof(float) * (size_t)n_seqs * L.nsig * (NBIN - 1));
     L.G_off = off;
     off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv * NCELL);
+    L.max_segs = n_seqs <= SEG_SCAN_MAX_SEQS ? (L.max_chunks + SCAN_SEG - 1) / SCAN_SEG : 0;
+    L.seg_off = off;
+    off = align256(off + sizeof(int32_t) * (size_t)n_seqs * n_kv * L.max_segs * NCELL);
     L.cnt_off = off;
     off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv);
     L.pos_off = off;
@@ -1014,7 +1078,14 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
       dominance_hist_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase,
                                                                           C, edges, G);
     }
-    dominance_scan_kernel<<<dim3(n_seqs * n_kv, NCELL / 256), 256, 0, stream>>>(G, cbase, n_kv);
+    if (L.max_segs > 0) {
+      int32_t* segsum = reinterpret_cast<int32_t*>(ws + L.seg_off);
+      const dim3 sgrid(n_seqs * n_kv, L.max_segs, NCELL / 256);
+      dominance_segsum_kernel<<<sgrid, 256, 0, stream>>>(G, cbase, n_seqs, n_kv, L.max_segs, segsum);
+      dominance_scan_kernel<<<sgrid, 256, 0, stream>>>(G, cbase, n_kv, L.max_segs, segsum);
+    } else {
+      dominance_scan_serial_kernel<<<dim3(n_seqs * n_kv, NCELL / 256), 256, 0, stream>>>(G, cbase, n_kv);
+    }
     if (n_kv <= 32) {
       survivor_all_kernel<<<L.max_chunks, 512, (size_t)n_kv * (NBIN - 1) * sizeof(float), stream>>>(
           xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges, G, k, cnt, recs);

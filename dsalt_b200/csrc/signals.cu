@@ -189,8 +189,13 @@ __global__ void __launch_bounds__(256) token_signals_wide_kernel(
     float* __restrict__ vnorm_out, float* __restrict__ logit_out) {
   constexpr int XN = Vec<XDT>::N;
   constexpr int VN = Vec<VDT>::N;
+  // gate weight of element i of chunk lane + 32 j at gws[(j * XN + i) * 32 + lane]: the lanes
+  // of a warp read consecutive doubles (no bank conflicts)
   extern __shared__ double gws[];
-  for (int i = threadIdx.x; i < d_model; i += blockDim.x) gws[i] = (double)load_elem(gate_w, i, gate_dt);
+  for (int e = threadIdx.x; e < d_model; e += blockDim.x) {
+    const int c = e / XN, i = e - c * XN, l = c & 31, j = c >> 5;
+    gws[(j * XN + i) * 32 + l] = (double)load_elem(gate_w, e, gate_dt);
+  }
   __syncthreads();
   // x is converted to the gate dtype before the product; for a gate in fp32 or in x's own
   // dtype that conversion is the identity, and one fp32->fp64 conversion serves both sums
@@ -222,19 +227,19 @@ __global__ void __launch_bounds__(256) token_signals_wide_kernel(
       if (j < xc) {
         float xv[XN];
         Vec<XDT>::unpack(xq[j], xv);
-        const int c = lane + 32 * j;
+        const double* gj = gws + j * XN * 32 + lane;
         if (xg_is_x) {
 #pragma unroll
           for (int i = 0; i < XN; ++i) {
             const double xd = (double)xv[i];
-            dot = __fma_rn(xd, gws[c * XN + i], dot);
+            dot = __fma_rn(xd, gj[i * 32], dot);
             sq = __fma_rn(xd, xd, sq);
           }
         } else {
 #pragma unroll
           for (int i = 0; i < XN; ++i) {
             const double xd = (double)xv[i];
-            dot = __fma_rn((double)round_to(xv[i], gate_dt), gws[c * XN + i], dot);
+            dot = __fma_rn((double)round_to(xv[i], gate_dt), gj[i * 32], dot);
             sq = __fma_rn(xd, xd, sq);
           }
         }
