@@ -266,8 +266,7 @@ def run_sharded(args, rank, world, local, dev):
     # dominant kernel: this rank's attention alone
     w, xn, vn = None, None, None
     out, lmk = core.forward(xs, gw, gb, alpha, qs)
-    from dsalt_b200.sharded import gather_signals
-    w, xn, vn = gather_signals(core._w, core._xn, core._vn, core.group, out=core._sig)
+    w, xn, vn = core._sig  # the whole sequence's signals, gathered by the step
     n_att = max(20, args.steps // 4)
     for _ in range(3):
         ops.attention_sharded(qs, core.k_ext, core.v_ext, p.q_pos0, p.kv_pos0, T, w, lmk, B, core.k_src, core.v_src,
@@ -318,8 +317,8 @@ def run_sharded(args, rank, world, local, dev):
                 "config": {"workload": CFG["workload"], "L": T, "heads": H, "head_dim": D, "d_model": CFG["dm"],
                            "k_lmk": k, "block": B, "n_min": CFG["n_min"], "n_max": CFG["n_max"],
                            "selection": "block_causal", "l2": "inputs larger than L2",
-                           "parallelism": f"sequence-sharded x{world} (NCCL all-gather of signals, halo send/recv, "
-                                          f"landmark rows over NVLink peer memory)"},
+                           "parallelism": f"sequence-sharded x{world} (signals, halo and landmark rows over NVLink "
+                                          f"peer memory between device-side barriers)"},
                 "clocks": clk.summary(), "device_status": status,
                 "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},

@@ -44,6 +44,9 @@ SIGNATURES = {
     "dsalt_attention_sharded_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I]),
     "dsalt_attention_fwd_sharded": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _I64, _I64, _I64, _I64,
                                          _P, _P, _P, _I, _I, _P, _P, _I64, _P, _I, _P, _P, _SZ, _P]),
+    "dsalt_peer_barrier": (_I, [_P, _P, _I, _I, _I, _P]),
+    "dsalt_peer_allgather": (_I, [_P, _P, _I, _I, _I64, _P]),
+    "dsalt_peer_copy": (_I, [_P, _P, _I64, _P]),
     "dsalt_ipc_export": (_I, [_P, _P, ctypes.POINTER(_I64)]),
     "dsalt_ipc_open": (_I, [_P, _I64, ctypes.POINTER(_P)]),
     "dsalt_ipc_close": (_I, [_P, _I64]),

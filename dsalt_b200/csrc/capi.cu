@@ -37,6 +37,11 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
                    int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
                    cudaStream_t stream, const ShardArgs* shard = nullptr);
 int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream);
+int launch_peer_barrier(int* own_flag, const int* const* flags, int n_ranks, int rank, int epoch, int* err,
+                        cudaStream_t stream);
+int launch_peer_allgather(void* dst, const void* const* src, int n_ranks, int rank, int64_t bytes_per_rank,
+                          cudaStream_t stream);
+int launch_peer_copy(void* dst, const void* src, int64_t bytes, cudaStream_t stream);
 
 // ---------------------------------------------------------------- errors
 static thread_local char g_err[512] = "";
@@ -258,6 +263,20 @@ int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int
   return launch_attn_tc(q, k, v, dtype, q_rows, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
                         lmk_block, nullptr, 1, tables, tables + 32, plan, q_rows / 128, out, out_dtype, lse,
                         device_status_ptr(), reinterpret_cast<cudaStream_t>(stream), &sa);
+}
+
+int dsalt_peer_barrier(int* own_flag, const int* const* peer_flags, int n_ranks, int rank, int epoch, void* stream) {
+  return launch_peer_barrier(own_flag, peer_flags, n_ranks, rank, epoch, device_status_ptr(),
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsalt_peer_allgather(void* dst, const void* const* src, int n_ranks, int rank, int64_t bytes_per_rank,
+                         void* stream) {
+  return launch_peer_allgather(dst, src, n_ranks, rank, bytes_per_rank, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsalt_peer_copy(void* dst, const void* src, int64_t bytes, void* stream) {
+  return launch_peer_copy(dst, src, bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 // device memory shared between the processes of one node (CUDA IPC, plain peer mappings)

@@ -6,18 +6,19 @@ positions; rank ``r`` owns queries ``[r·T_local, (r+1)·T_local)`` and computes
 projections outside this module. Per step:
 
 1. window widths and selection signals of the rank's own tokens (``dsalt_token_signals``);
-2. one NCCL all-gather of those compact signals (``w``, ``‖x‖``, value norms: 4·(2+H_kv)
-   bytes per token), so every rank holds them for the whole sequence;
+2. a device-side barrier across the GPUs, then every rank pulls the other ranks' compact
+   signals (``w``, ``‖x‖``, value norms: 4·(2+H_kv) bytes per token) over NVLink, so every
+   rank holds them for the whole sequence (or one grouped NCCL all-gather);
 3. the block-causal landmark sets of the rank's own 512-query blocks
    (``dsalt_select_block_range``: block ``b`` uses the prefix ``[0, b·512)``, as
    ``results/causal_landmark_check.py:176-186``);
-4. the window halo: the previous rank's last ``n_max - 1`` K/V rows, NCCL send/recv into
-   the rows in front of the local shard;
+4. the window halo: the previous rank's last ``n_max - 1`` K/V rows, copied into the rows
+   in front of the local shard;
 5. the attention of the local queries (``dsalt_attention_fwd_sharded``): window tiles from
    the halo-extended local K/V, landmark rows read directly from their owner's K/V shard
    over NVLink (CUDA IPC peer mappings, plain loads — no multicast);
-6. a closing NCCL all-reduce of one word, so that no rank overwrites its K/V shard while
-   another may still read landmark rows from it.
+6. a closing barrier, so that no rank overwrites its K/V shard or signals while another
+   may still read them.
 
 The output stays sharded (``[T_local, H, D]`` per rank). Results equal the single-GPU
 core on the whole sequence bit for bit (same kernels, same tiles).
@@ -119,12 +120,20 @@ def exchange_halo(k_ext: torch.Tensor, v_ext: torch.Tensor, plan: ShardPlan, hal
 class ShardedCore:
     """The core of one DSALT layer (widths, block-causal selection, attention) for one
     rank's shard of a sequence. ``k_local`` / ``v_local`` are the views the caller writes
-    its shard's post-RoPE keys / values into before :meth:`forward`."""
+    its shard's post-RoPE keys / values into before :meth:`forward`.
+
+    ``exchange="peer"`` (default) moves the signals and the halo over NVLink peer memory
+    between two device-side barriers (``dsalt_peer_barrier``); ``exchange="nccl"`` uses the
+    NCCL collectives of :func:`gather_signals` / :func:`exchange_halo` and a closing
+    all-reduce."""
 
     def __init__(self, seq_len: int, n_heads: int, n_kv: int, head_dim: int, k_lmk: int, n_min: int, n_max: int,
-                 block: int = 512, dtype=torch.bfloat16, group=None):
+                 block: int = 512, dtype=torch.bfloat16, group=None, exchange: str = "peer"):
         from . import ops
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'peer' or 'nccl'")
         self.ops = ops
+        self.exchange = exchange
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -135,71 +144,104 @@ class ShardedCore:
         self.k_lmk, self.n_min, self.n_max, self.block = k_lmk, n_min, n_max, block
         dev = torch.device("cuda", torch.cuda.current_device())
         p = self.plan
-        self.k_ext = torch.zeros(p.halo + p.t_local, n_kv, head_dim, dtype=dtype, device=dev)
+        T = p.t_local
+        self.k_ext = torch.zeros(p.halo + T, n_kv, head_dim, dtype=dtype, device=dev)
         self.v_ext = torch.zeros_like(self.k_ext)
         self.k_local = self.k_ext[p.halo:]
         self.v_local = self.v_ext[p.halo:]
-        self.out = torch.empty(p.t_local, n_heads, head_dim, dtype=dtype, device=dev)
-        self._w = torch.empty(p.t_local, dtype=torch.int32, device=dev)
-        self._xn = torch.empty(p.t_local, dtype=torch.float32, device=dev)
-        self._vn = torch.empty(p.t_local, n_kv, dtype=torch.float32, device=dev)
-        self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
-        L = seq_len
-        self._sig = (torch.empty(L, dtype=torch.int32, device=dev), torch.empty(L, dtype=torch.float32, device=dev),
-                     torch.empty(L, n_kv, dtype=torch.float32, device=dev))
+        self.out = torch.empty(T, n_heads, head_dim, dtype=dtype, device=dev)
+        # signals of the whole sequence; this rank writes its slice, the rest is gathered
+        self._sig = (torch.empty(seq_len, dtype=torch.int32, device=dev),
+                     torch.empty(seq_len, dtype=torch.float32, device=dev),
+                     torch.empty(seq_len, n_kv, dtype=torch.float32, device=dev))
+        sl = slice(p.q_pos0, p.q_pos0 + T)
+        self._w, self._xn, self._vn = self._sig[0][sl], self._sig[1][sl], self._sig[2][sl]
+        self._flag = torch.zeros(4, dtype=torch.int32, device=dev)
+        self._epoch = 0
         L_ = ops.L
         nsel = L_.query("dsalt_select_block_range_workspace_bytes", seq_len, n_heads, n_kv, k_lmk, block, p.set_hi)
-        natt = L_.query("dsalt_attention_sharded_workspace_bytes", p.t_local, n_heads, k_lmk, block, head_dim)
+        natt = L_.query("dsalt_attention_sharded_workspace_bytes", T, n_heads, k_lmk, block, head_dim)
         self._ws_sel = torch.empty(max(nsel, 1), dtype=torch.uint8, device=dev)
         self._ws_att = torch.empty(max(natt, 1), dtype=torch.uint8, device=dev)
         self._peers = []
         self._open_peers()
 
     def _open_peers(self):
-        """Peer pointer tables of every rank's K / V shard (CUDA IPC; own shard local)."""
-        mine = (self.ops.ipc_export(self.k_local), self.ops.ipc_export(self.v_local))
+        """Peer pointer tables (CUDA IPC; own entries local): K / V shards, the signal
+        arrays' slices, the barrier flags."""
+        T, r = self.plan.t_local, self.rank
+        bufs = [self.k_local, self.v_local, self._sig[0], self._sig[1], self._sig[2], self._flag]
+        mine = [self.ops.ipc_export(b) for b in bufs]
         allh = [None] * self.world
         dist.all_gather_object(allh, mine, group=self.group)
-        kp, vp = [], []
-        for r, ((kh, ko), (vh, vo)) in enumerate(allh):
-            if r == self.rank:
-                kp.append(self.k_local.data_ptr())
-                vp.append(self.v_local.data_ptr())
-            else:
-                kptr = self.ops.ipc_open(kh, ko)
-                vptr = self.ops.ipc_open(vh, vo)
-                self._peers += [(kptr, ko), (vptr, vo)]
-                kp.append(kptr)
-                vp.append(vptr)
+        tables = [[] for _ in bufs]
+        for j, handles in enumerate(allh):
+            for i, (h, off) in enumerate(handles):
+                if j == r:
+                    tables[i].append(bufs[i].data_ptr())
+                else:
+                    ptr = self.ops.ipc_open(h, off)
+                    self._peers.append((ptr, off))
+                    tables[i].append(ptr)
         dev = self.k_local.device
-        self.k_src = torch.tensor(kp, dtype=torch.int64, device=dev)
-        self.v_src = torch.tensor(vp, dtype=torch.int64, device=dev)
+        self._kp, self._vp = tables[0], tables[1]
+        self.k_src = torch.tensor(tables[0], dtype=torch.int64, device=dev)
+        self.v_src = torch.tensor(tables[1], dtype=torch.int64, device=dev)
+        # rank j's slice of each signal array
+        self._w_src = torch.tensor([a + j * T * 4 for j, a in enumerate(tables[2])], dtype=torch.int64, device=dev)
+        self._x_src = torch.tensor([a + j * T * 4 for j, a in enumerate(tables[3])], dtype=torch.int64, device=dev)
+        self._v_src = torch.tensor([a + j * T * self.n_kv * 4 for j, a in enumerate(tables[4])], dtype=torch.int64,
+                                   device=dev)
+        self._flags = torch.tensor(tables[5], dtype=torch.int64, device=dev)
 
     def close(self):
         for ptr, off in self._peers:
             self.ops.ipc_close(ptr, off)
         self._peers = []
 
+    def _barrier(self):
+        self._epoch += 1
+        L_, ops = self.ops.L, self.ops
+        L_.call("dsalt_peer_barrier", ops._ptr(self._flag), ops._ptr(self._flags), self.world, self.rank,
+                self._epoch, ops._stream())
+
     def forward(self, x, gate_weight, gate_bias, alpha, q):
         """``x [T_local, d_model]`` and ``q [T_local, H, D]`` of this rank's positions (``k_local`` /
-        ``v_local`` already written). Returns this rank's attention output ``[T_local, H, D]``."""
+        ``v_local`` already written). Returns this rank's attention output ``[T_local, H, D]``
+        and its landmark sets."""
         ops, p = self.ops, self.plan
         L = ops.L
-        # 1. own signals (value norms from the shard's values, as the single-GPU core)
-        L.call("dsalt_token_signals", ops._ptr(x), ops._dt(x), p.t_local, x.shape[1], x.stride(0),
+        T = p.t_local
+        # 1. own signals, into this rank's slice of the sequence arrays
+        L.call("dsalt_token_signals", ops._ptr(x), ops._dt(x), T, x.shape[1], x.stride(0),
                ops._ptr(gate_weight), ops._ptr(gate_bias), ops._dt(gate_weight), self.n_min, self.n_max,
                ops._ptr(self.v_local), ops._dt(self.v_local), self.v_local.stride(0), self.n_kv, self.head_dim,
                L.NORM_F32, ops._ptr(self._w), ops._ptr(self._xn), ops._ptr(self._vn), None, ops._stream())
-        # 2. all ranks' signals
-        w, xn, vn = gather_signals(self._w, self._xn, self._vn, self.group, out=self._sig)
-        # 3. landmark sets of the own blocks
+        w, xn, vn = self._sig
+        row_bytes = self.k_local.stride(0) * self.k_local.element_size()
+        if self.exchange == "peer":
+            # 2. every rank's signals and K / V are written
+            self._barrier()
+            # 3. the other ranks' signal slices and the window halo, over NVLink
+            for dst, src, n in ((w, self._w_src, T * 4), (xn, self._x_src, T * 4), (vn, self._v_src, T * self.n_kv * 4)):
+                L.call("dsalt_peer_allgather", ops._ptr(dst), ops._ptr(src), self.world, self.rank, n, ops._stream())
+            if p.halo > 0:
+                src_k = self._kp[self.rank - 1] + (T - p.halo) * row_bytes
+                src_v = self._vp[self.rank - 1] + (T - p.halo) * row_bytes
+                L.call("dsalt_peer_copy", ops._ptr(self.k_ext), src_k, p.halo * row_bytes, ops._stream())
+                L.call("dsalt_peer_copy", ops._ptr(self.v_ext), src_v, p.halo * row_bytes, ops._stream())
+        else:
+            gather_signals(self._w, self._xn, self._vn, self.group, out=self._sig)
+            exchange_halo(self.k_ext, self.v_ext, p, self.halo_next, self.group)
+        # 4. landmark sets of the own blocks
         lmk = ops.select_block_range(xn, vn, w, alpha, self.k_lmk, self.n_heads, self.block, p.set_lo, p.set_hi,
                                      workspace=self._ws_sel)
-        # 4. window halo from the previous rank
-        exchange_halo(self.k_ext, self.v_ext, p, self.halo_next, self.group)
-        # 5. attention of the own queries
+        # 5. attention of the own queries (landmark rows read from their owners)
         ops.attention_sharded(q, self.k_ext, self.v_ext, p.q_pos0, p.kv_pos0, p.seq_len, w, lmk, self.block,
                               self.k_src, self.v_src, p.t_local, out=self.out, workspace=self._ws_att)
-        # 6. every rank is done reading the others' K / V
-        dist.all_reduce(self._flag, group=self.group)
+        # 6. every rank is done reading the others' memory
+        if self.exchange == "peer":
+            self._barrier()
+        else:
+            dist.all_reduce(self._flag[:1], group=self.group)
         return self.out, lmk

@@ -152,6 +152,19 @@ int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int
                                 const void* const* lmk_k_src, const void* const* lmk_v_src, int64_t rows_per_src,
                                 void* out, int out_dtype, float* lse, void* workspace, size_t workspace_bytes,
                                 void* stream);
+/* dsalt_peer_barrier: rank `rank` of n_ranks GPUs (one process each) stores `epoch` in its
+ *   own flag (an int in its memory) and waits until every rank's flag (peer_flags: device
+ *   array of the ranks' flag pointers, peers mapped by dsalt_ipc_open) has reached it;
+ *   epochs must increase from call to call. Memory written on this GPU before the call is
+ *   visible to the peers' work queued after theirs. A wait longer than 2 s gives up and
+ *   sets the device status word (no hang).
+ * dsalt_peer_allgather: dst[j * bytes_per_rank ...] <- src[j][0 .. bytes_per_rank) for
+ *   every rank j != rank (src: device array of the ranks' pointers; 16-byte multiples).
+ * dsalt_peer_copy: bytes from src (this or a peer GPU's memory) to dst, on the stream. */
+int dsalt_peer_barrier(int* own_flag, const int* const* peer_flags, int n_ranks, int rank, int epoch, void* stream);
+int dsalt_peer_allgather(void* dst, const void* const* src, int n_ranks, int rank, int64_t bytes_per_rank,
+                         void* stream);
+int dsalt_peer_copy(void* dst, const void* src, int64_t bytes, void* stream);
 int dsalt_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
 int dsalt_ipc_open(const void* handle, int64_t offset, void** ptr_out);
 int dsalt_ipc_close(void* ptr, int64_t offset);

@@ -140,7 +140,7 @@ def test_sharded_kernels_equal_whole_sequence_on_emulated_shards():
     assert torch.equal(torch.cat(outs), full_out)
 
 
-def _gpu_rank_main(rank, world, port, out_q):
+def _gpu_rank_main(rank, world, port, out_q, exchange):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -152,7 +152,7 @@ def _gpu_rank_main(rank, world, port, out_q):
         from dsalt_b200.sharded import ShardedCore
         x, gw, gb, alpha, q, kk, v = _gpu_inputs(torch.device("cuda", rank))
         L, H, D, k, B = q.shape[0], q.shape[1], q.shape[2], 64, 512
-        core = ShardedCore(L, H, H, D, k, 16, 300, B)
+        core = ShardedCore(L, H, H, D, k, 16, 300, B, exchange=exchange)
         p = core.plan
         sl = slice(p.q_pos0, p.q_pos0 + p.t_local)
         core.k_local.copy_(kk[sl])
@@ -184,13 +184,14 @@ def _gpu_inputs(dev):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sharded_core_on_two_gpus_equals_single_gpu():
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_sharded_core_on_two_gpus_equals_single_gpu(exchange):
     from dsalt_b200 import ops
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gpu_rank_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_gpu_rank_main, args=(r, world, port, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
