@@ -556,27 +556,28 @@ __global__ void __launch_bounds__(256) dominance_hist_kernel(
   for (int i = threadIdx.x; i < NCELL; i += blockDim.x) out[i] = hist[i];
 }
 
-// The same grids for all kv groups of a chunk in one 512-thread CTA (n_kv <= 32): the
-// token loads, ‖x‖ bins and coverage tests are shared by the groups, and one CTA per chunk
-// amortises the latency of the scans. Shared memory: n_kv 32×32 grids + edges.
+// The same grids for gpb kv groups of a chunk per 512-thread CTA (n_kv <= 32): the token
+// loads, ‖x‖ bins and coverage tests are shared by the CTA's groups. Shared memory: gpb
+// 32×32 grids + edges.
 __global__ void __launch_bounds__(512) dominance_hist_all_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w, int n_kv,
     const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
-    const float* __restrict__ edges, int32_t* __restrict__ G) {
+    const float* __restrict__ edges, int32_t* __restrict__ G, int gpb) {
   // grids with rows padded to NBIN+1 entries, so that column scans hit distinct banks
   constexpr int RS = NBIN + 1;
   extern __shared__ int32_t hs[];
-  int32_t* hist = hs;                                            // [n_kv][NBIN][RS]
-  float* ev = reinterpret_cast<float*>(hs + n_kv * NBIN * RS);   // [n_kv][NBIN-1]
+  // this CTA: kv groups [g0, g0 + gpb) of chunk blockIdx.x
+  int32_t* hist = hs;                                            // [gpb][NBIN][RS]
+  float* ev = reinterpret_cast<float*>(hs + gpb * NBIN * RS);    // [gpb][NBIN-1]
   __shared__ float ex[NBIN - 1];
-  const int c = blockIdx.x, nsig = 1 + n_kv;
+  const int c = blockIdx.x, nsig = 1 + n_kv, g0 = blockIdx.y * gpb;
   const int total = base[n_seqs];
   if (c >= total) return;
   const int s = find_seq(base, n_seqs, c);
-  for (int i = threadIdx.x; i < n_kv * NBIN * RS; i += blockDim.x) hist[i] = 0;
+  for (int i = threadIdx.x; i < gpb * NBIN * RS; i += blockDim.x) hist[i] = 0;
   if (threadIdx.x < NBIN - 1) ex[threadIdx.x] = edges[((int64_t)s * nsig + 0) * (NBIN - 1) + threadIdx.x];
-  for (int i = threadIdx.x; i < n_kv * (NBIN - 1); i += blockDim.x)
-    ev[i] = edges[((int64_t)s * nsig + 1) * (NBIN - 1) + i];  // groups 1..n_kv are consecutive
+  for (int i = threadIdx.x; i < gpb * (NBIN - 1); i += blockDim.x)
+    ev[i] = edges[((int64_t)s * nsig + 1 + g0) * (NBIN - 1) + i];  // groups are consecutive
   __syncthreads();
   const int start = cu[s];
   const int p0 = (c - base[s]) * C;
@@ -586,15 +587,15 @@ __global__ void __launch_bounds__(512) dominance_hist_all_kernel(
     const int64_t t = start + p;
     const bool live = p < p1 && p >= w[t];
     const int bx = live ? bin_of(xn[t], ex) : 0;
-    for (int g = 0; g < n_kv; ++g) {
-      const int cell = live ? (g * NBIN + bin_of(vn[t * n_kv + g], ev + g * (NBIN - 1))) * RS + bx : -1;
+    for (int g = 0; g < gpb; ++g) {
+      const int cell = live ? (g * NBIN + bin_of(vn[t * n_kv + g0 + g], ev + g * (NBIN - 1))) * RS + bx : -1;
       const unsigned same = __match_any_sync(0xffffffffu, cell);
       if (cell >= 0 && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[cell], __popc(same));
     }
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int row = wid; row < n_kv * NBIN; row += nw) {  // suffix along x bins, row = (g, value bin)
+  for (int row = wid; row < gpb * NBIN; row += nw) {  // suffix along x bins, row = (g, value bin)
     int v = hist[row * RS + lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -604,7 +605,7 @@ __global__ void __launch_bounds__(512) dominance_hist_all_kernel(
     hist[row * RS + lane] = v;
   }
   __syncthreads();
-  for (int col = wid; col < n_kv * NBIN; col += nw) {  // suffix along value bins, col = (g, x bin)
+  for (int col = wid; col < gpb * NBIN; col += nw) {  // suffix along value bins, col = (g, x bin)
     const int g = col / NBIN, b = col % NBIN;
     int v = hist[(g * NBIN + lane) * RS + b];
 #pragma unroll
@@ -615,8 +616,8 @@ __global__ void __launch_bounds__(512) dominance_hist_all_kernel(
     hist[(g * NBIN + lane) * RS + b] = v;
   }
   __syncthreads();
-  int32_t* out = G + (int64_t)c * n_kv * NCELL;
-  for (int i = threadIdx.x; i < n_kv * NCELL; i += blockDim.x) out[i] = hist[(i / NBIN) * RS + (i % NBIN)];
+  int32_t* out = G + ((int64_t)c * n_kv + g0) * NCELL;
+  for (int i = threadIdx.x; i < gpb * NCELL; i += blockDim.x) out[i] = hist[(i / NBIN) * RS + (i % NBIN)];
 }
 
 // exclusive prefix over the chunks of each sequence, in place: G[c] <- Σ_{c'<c} G[c'].
@@ -744,24 +745,24 @@ __global__ void survivor_kernel(const float* __restrict__ xn, const float* __res
   if (threadIdx.x == 0) surv_cnt[(int64_t)c * n_kv + g] = carry;
 }
 
-// survivor_kernel for all kv groups of a chunk in one 512-thread CTA (n_kv <= 32); the
+// survivor_kernel for gpb kv groups of a chunk per 512-thread CTA (n_kv <= 32); the
 // records of a (chunk, group) are compacted in no particular order (the selection does not
 // depend on it)
 __global__ void __launch_bounds__(512) survivor_all_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w, int n_kv,
     const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
     const float* __restrict__ edges, const int32_t* __restrict__ D, int k, int32_t* __restrict__ surv_cnt,
-    int4* __restrict__ surv_rec) {
-  extern __shared__ float es[];  // [n_kv][NBIN-1]
+    int4* __restrict__ surv_rec, int gpb) {
+  extern __shared__ float es[];  // [gpb][NBIN-1]
   __shared__ float ex[NBIN - 1];
   __shared__ int32_t cnt[32];
-  const int c = blockIdx.x, nsig = 1 + n_kv;
+  const int c = blockIdx.x, nsig = 1 + n_kv, g0 = blockIdx.y * gpb;
   const int total = base[n_seqs];
   if (c >= total) return;
   const int s = find_seq(base, n_seqs, c);
   if (threadIdx.x < NBIN - 1) ex[threadIdx.x] = edges[((int64_t)s * nsig + 0) * (NBIN - 1) + threadIdx.x];
-  for (int i = threadIdx.x; i < n_kv * (NBIN - 1); i += blockDim.x)
-    es[i] = edges[((int64_t)s * nsig + 1) * (NBIN - 1) + i];
+  for (int i = threadIdx.x; i < gpb * (NBIN - 1); i += blockDim.x)
+    es[i] = edges[((int64_t)s * nsig + 1 + g0) * (NBIN - 1) + i];
   if (threadIdx.x < 32) cnt[threadIdx.x] = 0;
   __syncthreads();
   const int start = cu[s];
@@ -774,12 +775,13 @@ __global__ void __launch_bounds__(512) survivor_all_kernel(
     const bool live = p < p1 && p >= w[t];
     const float xv = live ? xn[t] : 0.0f;
     const int bx = live ? bin_of(xv, ex) : 0;
-    for (int g = 0; g < n_kv; ++g) {
+    for (int gl = 0; gl < gpb; ++gl) {
+      const int g = g0 + gl;
       bool keep = false;
       int4 rec;
       if (live) {
         const float vv = vn[t * n_kv + g];
-        const int a = bin_of(vv, es + g * (NBIN - 1));
+        const int a = bin_of(vv, es + gl * (NBIN - 1));
         const int cell = (a == NBIN - 1 || bx == NBIN - 1) ? -1 : (a + 1) * NBIN + (bx + 1);
         const int dom = cell < 0 ? 0 : D[((int64_t)c * n_kv + g) * NCELL + cell];
         keep = dom < k;
@@ -787,13 +789,13 @@ __global__ void __launch_bounds__(512) survivor_all_kernel(
       }
       const unsigned ball = __ballot_sync(0xffffffffu, keep);
       int slot0 = 0;
-      if (lane == 0 && ball) slot0 = atomicAdd(&cnt[g], __popc(ball));
+      if (lane == 0 && ball) slot0 = atomicAdd(&cnt[gl], __popc(ball));
       slot0 = __shfl_sync(0xffffffffu, slot0, 0);
       if (keep) surv_rec[((int64_t)c * n_kv + g) * C + slot0 + __popc(ball & ((1u << lane) - 1))] = rec;
     }
   }
   __syncthreads();
-  if (threadIdx.x < n_kv) surv_cnt[(int64_t)c * n_kv + threadIdx.x] = cnt[threadIdx.x];
+  if (threadIdx.x < gpb) surv_cnt[(int64_t)c * n_kv + g0 + threadIdx.x] = cnt[threadIdx.x];
 }
 
 // per (block set, head): exact scores of the surviving candidates of earlier chunks
@@ -1070,10 +1072,12 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
     int32_t* cnt = reinterpret_cast<int32_t*>(ws + L.cnt_off);
     int4* recs = reinterpret_cast<int4*>(ws + L.pos_off);
     block_stats_kernel<<<dim3(n_seqs, nsig), 256, 0, stream>>>(part, cu, n_seqs, cbase, nsig, C, stats, edges);
+    // kv groups per CTA: 4 when they divide evenly (more CTAs in flight per SM)
+    const int gpb = n_kv % 4 == 0 ? 4 : (n_kv % 2 == 0 ? 2 : 1);
     if (n_kv <= 32) {
-      const size_t smh = (size_t)n_kv * (NBIN * (NBIN + 1) * sizeof(int32_t) + (NBIN - 1) * sizeof(float));
-      dominance_hist_all_kernel<<<L.max_chunks, 512, smh, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
-                                                                     edges, G);
+      const size_t smh = (size_t)gpb * (NBIN * (NBIN + 1) * sizeof(int32_t) + (NBIN - 1) * sizeof(float));
+      dominance_hist_all_kernel<<<dim3(L.max_chunks, n_kv / gpb), 512, smh, stream>>>(xnorm, vnorm, w, n_kv, cu,
+                                                                                      n_seqs, cbase, C, edges, G, gpb);
     } else {
       dominance_hist_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase,
                                                                           C, edges, G);
@@ -1087,8 +1091,8 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
       dominance_scan_serial_kernel<<<dim3(n_seqs * n_kv, NCELL / 256), 256, 0, stream>>>(G, cbase, n_kv);
     }
     if (n_kv <= 32) {
-      survivor_all_kernel<<<L.max_chunks, 512, (size_t)n_kv * (NBIN - 1) * sizeof(float), stream>>>(
-          xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges, G, k, cnt, recs);
+      survivor_all_kernel<<<dim3(L.max_chunks, n_kv / gpb), 512, (size_t)gpb * (NBIN - 1) * sizeof(float), stream>>>(
+          xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C, edges, G, k, cnt, recs, gpb);
     } else {
       survivor_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
                                                                     edges, G, k, cnt, recs);
