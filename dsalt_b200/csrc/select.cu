@@ -36,8 +36,8 @@ constexpr int STAT_CHUNK = 512;          // tokens per partial sum in whole-sequ
 constexpr int SEL_THREADS = 512;
 constexpr int KEY_CAP = 8192;            // candidate keys cached in shared memory
 constexpr int BSEL_THREADS = 256;        // block-causal select: small CTAs, several per SM
-constexpr int BSEL_KEY_CAP = 2048;       // its key cache (the prefix-dominance filter keeps ~1K)
-constexpr int BSEL_REC_CAP = 8192;       // survivors whose chunk index is tabulated
+constexpr int BSEL_KEY_CAP = 1536;       // its key cache (the prefix-dominance filter keeps ~1K)
+constexpr int BSEL_REC_CAP = 4608;       // survivors whose chunk index is tabulated
 constexpr int MAX_K = 1024;
 
 // thresholds (in units of the sequence's std above its mean) of the dominance grid:
@@ -799,7 +799,7 @@ __global__ void __launch_bounds__(512) survivor_all_kernel(
 }
 
 // per (block set, head): exact scores of the surviving candidates of earlier chunks
-__global__ void __launch_bounds__(BSEL_THREADS) block_select_kernel(
+__global__ void __launch_bounds__(BSEL_THREADS, 6) block_select_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w,
     const float* __restrict__ alpha, const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base,
     int C, int n_heads, int n_kv, int k, const double2* __restrict__ stats, const int32_t* __restrict__ D,
