@@ -9,14 +9,15 @@
 //
 // Work item = (128-query tile, head); persistent CTAs, one per SM. Per item the key
 // axis is a band of 128-key window tiles ending at the tile's last row and reaching back
-// to max(0, m0 − max_w + 1), plus ceil(k/128) landmark tiles; the window tiles go from
-// the diagonal one leftwards, then the landmark tiles. Each CTA runs two independent
-// pipelines (A, B) on alternate items; a pipeline is
+// to max(0, m0 − max_w + 1), plus ceil(k/128) landmark tiles; the order is the diagonal
+// window tile, the landmark tiles, then the other window tiles leftwards. Each CTA runs
+// two independent pipelines (A, B) on alternate items; a pipeline is
 //   a producer warp   TMA (no multicast) of the Q tile and the K/V window tiles into a
 //                     3-stage K ring and a 2-stage V ring; landmark K/V rows gathered with
 //                     cp.async into the same rings (replaces _build_landmark_kv,
-//                     selectors.py:137-159); it fills the next item's description slot
-//                     while the current item's last gather is in flight;
+//                     selectors.py:137-159); it publishes the next item's description
+//                     slot during the current item and prefetches that item's landmark
+//                     rows into L2;
 //   an MMA warp       one thread issues S = Q·Kᵀ (SS form) into TMEM and O += P·V (TS
 //                     form: P read from TMEM, V from smem) into a TMEM accumulator;
 //   4 softmax warps   row r ↔ TMEM lane r: the S row is read once into registers,
@@ -161,11 +162,16 @@ __device__ __forceinline__ Item make_item(const Params& p, int item, int4 a, int
   return f;
 }
 
-// Processing order of an item's key tiles: the window tiles from the diagonal one leftwards
-// (every valid row gets a finite running max on the first tile), then the landmark tiles.
+// Processing order of an item's key tiles: the diagonal window tile (every valid row gets a
+// finite running max on the first tile), the landmark tiles, then the other window tiles
+// leftwards. The landmark rows are gathered with cp.async while the diagonal tile's softmax
+// runs; the leftmost window tile is often nearly empty and would not cover the gather.
 // Returns the window-tile index, or -1 - (landmark tile).
 __device__ __forceinline__ int tile_at(const Item& f, int t) {
-  return t < f.nwt ? f.nwt - 1 - t : -1 - (t - f.nwt);
+  if (f.nwt == 0) return -1 - t;
+  if (t == 0) return f.nwt - 1;
+  if (t <= f.nlt) return -t;
+  return f.nwt - 1 - (t - f.nlt);
 }
 
 template <int HD>
@@ -357,6 +363,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         cp_async_mbar_arrive(&B.it_full[sl]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&B.it_full[sl]);
+        // the item's landmark rows are gathered an item later: bring them into L2 now
+        // (scattered 128-byte rows; the gather would otherwise wait on DRAM latency)
+        if (fn.nlt > 0 && p.shard_tiles == 0) {
+          for (int c = lane; c < p.k_lmk; c += 32) {
+            const int pos = __ldg(P + c);
+            if (pos >= 0) {
+              const int64_t off = (int64_t)(fn.kvb + pos) * p.kv_stride + (int64_t)fn.hk * HD;
+              prefetch_l2(kg + off);
+              prefetch_l2(vg + off);
+            }
+          }
+        }
         return true;
       };
       int g = 0, it = 0;
@@ -387,19 +405,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         f.qb + f.m0);
         }
         const int NK = f.nwt + f.nlt;
-        // the landmark rows are gathered after the window tiles: bring them into L2 now
-        // (scattered 128-byte rows; the gather would otherwise wait on DRAM latency)
-        if (f.nlt > 0 && p.shard_tiles == 0) {
-          if (!mbar_wait(&B.it_full[sl_i], (uint32_t)(it / NIS) & 1, p.err, 15)) break;
-          for (int c = lane; c < p.k_lmk; c += 32) {
-            const int pos = S.pos[c];
-            if (pos >= 0) {
-              const int64_t off = (int64_t)(f.kvb + pos) * p.kv_stride + (int64_t)f.hk * HD;
-              prefetch_l2(kg + off);
-              prefetch_l2(vg + off);
-            }
-          }
-        }
         for (int t = 0; t < NK; ++t, ++g) {
           if (t == 1 && !published) {
             if (!publish(item_n, it + 1, an, bn)) { ok = false; break; }
