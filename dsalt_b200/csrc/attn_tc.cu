@@ -80,6 +80,7 @@ struct Params {
   uint32_t idesc_qk, idesc_pv;
   void* out;
   int out_dtype;
+  int out_v8;  // out is 32-byte aligned: rows written with 32-byte stores
   float* lse;
   int* err;
 };
@@ -242,6 +243,31 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+
+// Masks the 32 columns c0 + e of a chunk outside the row's valid range [a, b]:
+// x = min(x, t1, t2) with the exact thresholds t1(c) = C(c − a + ½) = C·c + A1 and
+// t2(c) = C(b + ½ − c) = −C·c + A2, stepped two columns at a time by packed adds of ±2C
+// (exact: the thresholds stay half-integers times 2^100)
+__device__ __forceinline__ void mask_chunk(float* xc, float c0f, float A1, float A2) {
+  uint64_t t1 = pk2(fmaf(MASK_C, c0f, A1), fmaf(MASK_C, c0f + 1.0f, A1));
+  uint64_t t2 = pk2(fmaf(-MASK_C, c0f, A2), fmaf(-MASK_C, c0f + 1.0f, A2));
+  const uint64_t d1 = pk2(2.0f * MASK_C, 2.0f * MASK_C), d2 = pk2(-2.0f * MASK_C, -2.0f * MASK_C);
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    const float2 u1 = up2(t1), u2 = up2(t2);
+    xc[e] = fmin3f(xc[e], u1.x, u2.x);
+    xc[e + 1] = fmin3f(xc[e + 1], u1.y, u2.y);
+    t1 = add2(t1, d1);
+    t2 = add2(t2, d2);
+  }
+}
+
+// 32-byte store (sm_100); the address must be 32-byte aligned
+__device__ __forceinline__ void st_global_v8(void* ptr, const uint32_t* r) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(__cvta_generic_to_global(ptr)),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
 }
 
 struct PipeBars {
@@ -645,11 +671,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               for (int e = 0; e < 16; ++e) pk[e] = 0u;
             } else {
               float* xc = x + c0;
-              if (!((all >> cc) & 1)) {
-#pragma unroll
-                for (int e = 0; e < 32; ++e)
-                  xc[e] = fmin3f(xc[e], fmaf(MASK_C, (float)(c0 + e), A1), fmaf(-MASK_C, (float)(c0 + e), A2));
-              }
+              if (!((all >> cc) & 1)) mask_chunk(xc, (float)c0, A1, A2);
               float c0m = fmax3f(xc[0], xc[1], xc[2]), c1m = fmax3f(xc[3], xc[4], xc[5]);
 #pragma unroll
               for (int e = 6; e < 30; e += 4) {
@@ -689,11 +711,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int c0 = cc * 32;
             if ((none >> cc) & 1) continue;
             float* xc = x + c0;
-            if (!((all >> cc) & 1)) {
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                xc[e] = fmin3f(xc[e], fmaf(MASK_C, (float)(c0 + e), A1), fmaf(-MASK_C, (float)(c0 + e), A2));
-            }
+            if (!((all >> cc) & 1)) mask_chunk(xc, (float)c0, A1, A2);
 #pragma unroll
             for (int e = 0; e < 32; e += 4) {
               m0 = fmax3f(m0, xc[e], xc[e + 1]);
@@ -775,23 +793,30 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const bool good = l > 1e-9f;
         const float inv = good ? 1.0f / l : 0.0f;
         const int64_t row = (int64_t)f.qb + i;
-        if (p.out_dtype == DSALT_F32) {
-          float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (row * p.H + f.h) * HD);
+        // the row's HD outputs, as 32-bit words (fp32 values or 16-bit pairs)
+        const bool f32o = p.out_dtype == DSALT_F32;
+        if (f32o) {
 #pragma unroll
-          for (int d = 0; d < HD; d += 4)
-            o[d / 4] = make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+          for (int d = 0; d < HD; ++d) acc[d] *= inv;
         } else {
-          uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + (row * p.H + f.h) * HD);
           const bool bo = p.out_dtype == DSALT_BF16;
 #pragma unroll
-          for (int d = 0; d < HD; d += 8) {
-            uint4 q4;
-            q4.x = bo ? pack_bf16x2(acc[d] * inv, acc[d + 1] * inv) : pack_f16x2(acc[d] * inv, acc[d + 1] * inv);
-            q4.y = bo ? pack_bf16x2(acc[d + 2] * inv, acc[d + 3] * inv) : pack_f16x2(acc[d + 2] * inv, acc[d + 3] * inv);
-            q4.z = bo ? pack_bf16x2(acc[d + 4] * inv, acc[d + 5] * inv) : pack_f16x2(acc[d + 4] * inv, acc[d + 5] * inv);
-            q4.w = bo ? pack_bf16x2(acc[d + 6] * inv, acc[d + 7] * inv) : pack_f16x2(acc[d + 6] * inv, acc[d + 7] * inv);
-            o[d / 8] = q4;
+          for (int d = 0; d < HD; d += 2) {
+            const uint32_t w2 = bo ? pack_bf16x2(acc[d] * inv, acc[d + 1] * inv) : pack_f16x2(acc[d] * inv, acc[d + 1] * inv);
+            acc[d / 2] = __uint_as_float(w2);
           }
+        }
+        const uint32_t* wv = reinterpret_cast<const uint32_t*>(acc);
+        char* orow = reinterpret_cast<char*>(p.out) + (row * p.H + f.h) * (int64_t)HD * (f32o ? 4 : 2);
+        const int nw = f32o ? HD : HD / 2;
+        if (p.out_v8) {
+#pragma unroll
+          for (int q = 0; q < HD; q += 8)
+            if (q < nw) st_global_v8(orow + q * 4, wv + q);
+        } else {
+#pragma unroll
+          for (int q = 0; q < HD; q += 4)
+            if (q < nw) *reinterpret_cast<uint4*>(orow + q * 4) = make_uint4(wv[q], wv[q + 1], wv[q + 2], wv[q + 3]);
         }
         const float mm = (m_acc == -INFINITY) ? 0.0f : m_acc;
         if (p.lse) p.lse[row * p.H + f.h] = good ? (mm + log2f(l)) * 0.6931471805599453f : -INFINITY;
@@ -942,6 +967,7 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   p.idesc_pv = umma_idesc_f16(ab, 0, 1, BM, HD);
   p.out = out;
   p.out_dtype = out_dtype;
+  p.out_v8 = ((uintptr_t)out & 31) == 0 ? 1 : 0;
   p.lse = lse;
   p.err = err;
   int dev = 0, nsm = 148;
