@@ -662,6 +662,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const float mu = (m_acc == -INFINITY) ? 0.0f : m_acc;
           const uint64_t sl2 = pk2(sl, sl), nmu2 = pk2(-mu, -mu);
           float cm = -INFINITY;
+          uint32_t pk0[16];  // chunk 0's P, stored with chunk 1's (the previous P·V has more time)
 #pragma unroll
           for (int cc = 0; cc < BN / 32; ++cc) {
             const int c0 = cc * 32;
@@ -691,12 +692,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 pk[(e >> 1) + 1] = pack_p(bf, p2, p3);
               }
             }
+            if (cc == 0) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) pk0[e] = pk[e];
+              continue;
+            }
             if (!p_free) {
               // previous P·V done: the P buffer may be overwritten
               if (!mbar_wait(B.o_full, (u - 1) & 1, p.err, 33)) { ok = false; break; }
               tc_fence_after();
               p_free = true;
             }
+            if (cc == 1) DSALT_TMEM_ST16(tP, pk0);
             DSALT_TMEM_ST16(tP + cc * 16, pk);
           }
           if (!ok) break;
