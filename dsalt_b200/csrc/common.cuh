@@ -195,6 +195,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// 1-D bulk copy global -> this CTA's shared memory (no multicast); completion counted in
+// bytes on the mbarrier. Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_dst),
+               "l"(__cvta_generic_to_global(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // cp.async (16 bytes, zero-filled when src_bytes == 0) and its mbarrier tracking
 __device__ __forceinline__ void cp_async_16(uint32_t smem_addr, const void* gmem, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(__cvta_generic_to_global(gmem)),

@@ -13,6 +13,8 @@
 //    rounded to the input dtype.
 // One warp per token; 16-byte vector loads; HBM-bound (reads x and v once). The wide
 // variant issues all of a token's loads up front (enough bytes in flight for HBM rate).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace dsalt {
@@ -176,6 +178,72 @@ __device__ __forceinline__ void ldg16x4(const uint4* q0, const uint4* q1, const 
       : "l"(p0), "l"(p1), "l"(p2), "l"(p3));
 }
 
+// The reductions of one token held as XCM / VCM 16-byte chunks per lane (chunk j of lane l
+// = row bytes [16 (l + 32 j), 16 (l + 32 j) + 16)): the gate logit and width, ‖x‖ and the
+// per-head ‖v‖, in fp64 with a fixed accumulation order.
+template <int XDT, int VDT, int XCM, int VCM>
+__device__ __forceinline__ void reduce_token(const uint4* xq, const uint4* vq, const double* gws, int lane, int xc,
+                                             int vc, int vcpg, bool xg_is_x, int gate_dt, double bias, int n_min,
+                                             int n_max, int norm_mode, int n_kv, int64_t t, int32_t* w_out,
+                                             float* xnorm_out, float* vnorm_out, float* logit_out) {
+  constexpr int XN = Vec<XDT>::N;
+  constexpr int VN = Vec<VDT>::N;
+  double dot = 0.0, sq = 0.0;
+#pragma unroll
+  for (int j = 0; j < XCM; ++j) {
+    if (j < xc) {
+      float xv[XN];
+      Vec<XDT>::unpack(xq[j], xv);
+      const double* gj = gws + j * XN * 32 + lane;
+      if (xg_is_x) {
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+          const double xd = (double)xv[i];
+          dot = __fma_rn(xd, gj[i * 32], dot);
+          sq = __fma_rn(xd, xd, sq);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+          const double xd = (double)xv[i];
+          dot = __fma_rn((double)round_to(xv[i], gate_dt), gj[i * 32], dot);
+          sq = __fma_rn(xd, xd, sq);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  }
+  if (lane == 0) {
+    const float logit = f64_to(dot + bias, gate_dt);
+    w_out[t] = width_from_logit(logit, gate_dt, n_min, n_max);
+    if (logit_out) logit_out[t] = logit;
+    float xn = sqrtf(__double2float_rn(sq));
+    if (norm_mode == DSALT_NORM_INPUT) xn = round_to(xn, XDT);
+    xnorm_out[t] = xn;
+  }
+#pragma unroll
+  for (int j = 0; j < VCM; ++j) {
+    if (j < vc) {
+      float vv[VN];
+      Vec<VDT>::unpack(vq[j], vv);
+      double s = 0.0;
+#pragma unroll
+      for (int i = 0; i < VN; ++i) s = __fma_rn((double)vv[i], (double)vv[i], s);
+      for (int o = vcpg >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const int c = lane + 32 * j;
+      if ((c % vcpg) == 0) {
+        float vn = sqrtf(__double2float_rn(s));
+        if (norm_mode == DSALT_NORM_INPUT) vn = round_to(vn, VDT);
+        vnorm_out[t * n_kv + c / vcpg] = vn;
+      }
+    }
+  }
+}
+
 // Same arithmetic (and accumulation order) as token_signals_kernel, for 16-bit x and v
 // whose rows split into at most XCM (x) / VCM (v) 16-byte chunks per lane: every load of
 // a token is issued before any is used, so a warp keeps its whole token (up to 8 KB) in
@@ -221,60 +289,82 @@ __global__ void __launch_bounds__(256) token_signals_wide_kernel(
     for (int j = 0; j < VCM; j += 4)
       ldg16x4(vr + lane + 32 * (j < vc ? j : 0), vr + lane + 32 * (j + 1 < vc ? j + 1 : 0),
               vr + lane + 32 * (j + 2 < vc ? j + 2 : 0), vr + lane + 32 * (j + 3 < vc ? j + 3 : 0), vq + j);
-    double dot = 0.0, sq = 0.0;
-#pragma unroll
-    for (int j = 0; j < XCM; ++j) {
-      if (j < xc) {
-        float xv[XN];
-        Vec<XDT>::unpack(xq[j], xv);
-        const double* gj = gws + j * XN * 32 + lane;
-        if (xg_is_x) {
-#pragma unroll
-          for (int i = 0; i < XN; ++i) {
-            const double xd = (double)xv[i];
-            dot = __fma_rn(xd, gj[i * 32], dot);
-            sq = __fma_rn(xd, xd, sq);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < XN; ++i) {
-            const double xd = (double)xv[i];
-            dot = __fma_rn((double)round_to(xv[i], gate_dt), gj[i * 32], dot);
-            sq = __fma_rn(xd, xd, sq);
-          }
-        }
-      }
+    reduce_token<XDT, VDT, XCM, VCM>(xq, vq, gws, lane, xc, vc, vcpg, xg_is_x, gate_dt, bias, n_min, n_max, norm_mode,
+                                     n_kv, t, w_out, xnorm_out, vnorm_out, logit_out);
+  }
+}
+
+// The same per-token reductions with the rows streamed through shared memory by 1-D bulk
+// copies: each warp keeps `stages` tokens in flight (its x and v rows, xc·512 + vc·512
+// bytes each) besides the one it reduces. Lane 0 of a warp issues its copies; the warp
+// waits on the stage's barrier (bounded), reads the rows from shared memory (lane l reads
+// chunks l + 32 j: no bank conflicts), refills the stage and then reduces. With the
+// reductions removed this streams x and v at the HBM copy rate; with them the kernel is
+// bound by the fp64 reductions (exact sums), not by memory.
+// Shared memory: gate weights (fp64) | barriers [warp][stage] | rows [warp][stage].
+template <int XDT, int VDT, int XCM, int VCM>
+__global__ void __launch_bounds__(1024) token_signals_bulk_kernel(
+    const void* __restrict__ x, int64_t T, int d_model, int64_t x_stride, const void* __restrict__ gate_w,
+    const void* __restrict__ gate_b, int gate_dt, int n_min, int n_max, const void* __restrict__ v, int64_t v_stride,
+    int n_kv, int head_dim, int norm_mode, int32_t* __restrict__ w_out, float* __restrict__ xnorm_out,
+    float* __restrict__ vnorm_out, float* __restrict__ logit_out, int stages, int* __restrict__ err) {
+  constexpr int XN = Vec<XDT>::N;
+  constexpr int VN = Vec<VDT>::N;
+  extern __shared__ __align__(128) unsigned char sig_smem[];
+  double* gws = reinterpret_cast<double*>(sig_smem);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int xc = d_model / XN / 32, vcpg = head_dim / VN, vc = n_kv * vcpg / 32;
+  const uint32_t xbytes = (uint32_t)xc * 512, vbytes = (uint32_t)vc * 512, sbytes = xbytes + vbytes;
+  const size_t gws_bytes = ((size_t)d_model * 8 + 127) & ~(size_t)127;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sig_smem + gws_bytes) + warp * stages;
+  unsigned char* rows = sig_smem + gws_bytes + (((size_t)wpb * stages * 8 + 127) & ~(size_t)127) +
+                        (size_t)warp * stages * sbytes;
+  for (int e = threadIdx.x; e < d_model; e += blockDim.x) {
+    const int c = e / XN, i = e - c * XN, l = c & 31, j = c >> 5;
+    gws[(j * XN + i) * 32 + l] = (double)load_elem(gate_w, e, gate_dt);
+  }
+  if (lane == 0)
+    for (int st = 0; st < stages; ++st) mbar_init(bars + st, 1);
+  fence_barrier_init();
+  __syncthreads();
+  const bool xg_is_x = gate_dt == DSALT_F32 || gate_dt == XDT;
+  const double bias = (double)load_elem(gate_b, 0, gate_dt);
+  const int64_t warp0 = (int64_t)blockIdx.x * wpb + warp, nwarps = (int64_t)gridDim.x * wpb;
+  auto issue = [&](int64_t t, int st) {
+    mbar_arrive_expect_tx(bars + st, sbytes);
+    const uint32_t dst = smem_u32(rows + (size_t)st * sbytes);
+    bulk_load(dst, elem_ptr<XDT>(x, t * x_stride), xbytes, bars + st);
+    bulk_load(dst + xbytes, elem_ptr<VDT>(v, t * v_stride), vbytes, bars + st);
+  };
+  if (lane == 0)
+    for (int st = 0; st < stages; ++st)
+      if (warp0 + st * nwarps < T) issue(warp0 + st * nwarps, st);
+  int k = 0;
+  for (int64_t t = warp0; t < T; t += nwarps, ++k) {
+    const int st = k % stages;
+    if (!mbar_wait(bars + st, (uint32_t)(k / stages) & 1, err, 50)) {
+      // give the warp's copies still in flight (tokens k .. k + stages - 1) a bounded
+      // chance to land before the block exits
+      for (int q = k + 1; q < k + stages; ++q)
+        if (warp0 + q * nwarps < T) mbar_wait(bars + q % stages, (uint32_t)(q / stages) & 1, err, 51, 100000000ull);
+      break;
     }
+    const uint4* xs = reinterpret_cast<const uint4*>(rows + (size_t)st * sbytes);
+    const uint4* vs = reinterpret_cast<const uint4*>(rows + (size_t)st * sbytes + xbytes);
+    uint4 xq[XCM], vq[VCM];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    }
-    if (lane == 0) {
-      const float logit = f64_to(dot + bias, gate_dt);
-      w_out[t] = width_from_logit(logit, gate_dt, n_min, n_max);
-      if (logit_out) logit_out[t] = logit;
-      float xn = sqrtf(__double2float_rn(sq));
-      if (norm_mode == DSALT_NORM_INPUT) xn = round_to(xn, XDT);
-      xnorm_out[t] = xn;
-    }
+    for (int j = 0; j < XCM; ++j) xq[j] = xs[lane + 32 * (j < xc ? j : 0)];
 #pragma unroll
-    for (int j = 0; j < VCM; ++j) {
-      if (j < vc) {
-        float vv[VN];
-        Vec<VDT>::unpack(vq[j], vv);
-        double s = 0.0;
-#pragma unroll
-        for (int i = 0; i < VN; ++i) s = __fma_rn((double)vv[i], (double)vv[i], s);
-        for (int o = vcpg >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        const int c = lane + 32 * j;
-        if ((c % vcpg) == 0) {
-          float vn = sqrtf(__double2float_rn(s));
-          if (norm_mode == DSALT_NORM_INPUT) vn = round_to(vn, VDT);
-          vnorm_out[t * n_kv + c / vcpg] = vn;
-        }
-      }
+    for (int j = 0; j < VCM; ++j) vq[j] = vs[lane + 32 * (j < vc ? j : 0)];
+    __syncwarp();
+    // every lane has read the stage: refill it with the warp's token `stages` steps ahead
+    // (the generic-proxy reads are ordered before the copy's async-proxy writes)
+    if (lane == 0 && t + stages * nwarps < T) {
+      fence_proxy_async_smem();
+      issue(t + stages * nwarps, st);
     }
+    reduce_token<XDT, VDT, XCM, VCM>(xq, vq, gws, lane, xc, vc, vcpg, xg_is_x, gate_dt, bias, n_min, n_max, norm_mode,
+                                     n_kv, t, w_out, xnorm_out, vnorm_out, logit_out);
   }
 }
 
@@ -309,8 +399,46 @@ int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int
   const int xc = d_model / xvec, vcpg = head_dim / vvec, vtot = n_kv * vcpg;
   if (xes == 2 && x_dtype == v_dtype && xc % 32 == 0 && xc / 32 <= 8 && vcpg <= 32 && vtot % 32 == 0 &&
       vtot / 32 <= 8 && d_model <= 6144) {
-    const size_t smem = (size_t)d_model * sizeof(double);
     const bool x4 = xc / 32 <= 4, v4 = vtot / 32 <= 4;
+    // bulk-copy path: 32 warps per block, one block per SM, one token in flight per warp
+    // besides the one it reduces, when the rows fit in 200 KB of shared memory
+    {
+      const size_t sbytes = (size_t)(xc + vtot) * 16;
+      const size_t gws_bytes = ((size_t)d_model * 8 + 127) & ~(size_t)127;
+      const int wpb = 32, stages = 1;
+      const size_t smem_b = gws_bytes + (((size_t)wpb * stages * 8 + 127) & ~(size_t)127) + (size_t)wpb * stages * sbytes;
+      if (smem_b <= 200 * 1024) {
+        int dev = 0, nsm = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        const int64_t bblocks = std::min<int64_t>((T + wpb - 1) / wpb, nsm);
+        int rc = DSALT_OK;
+#define DSALT_SIG_BULK(DT, XC, VC)                                                                                   \
+  do {                                                                                                                \
+    auto kern = token_signals_bulk_kernel<DT, DT, XC, VC>;                                                            \
+    if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b),      \
+                         "token_signals smem attr")))                                                                 \
+      return rc;                                                                                                      \
+    kern<<<(unsigned)bblocks, wpb * 32, smem_b, stream>>>(x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, \
+                                                         n_max, v, v_stride, n_kv, head_dim, norm_mode, w_out,         \
+                                                         xnorm_out, vnorm_out, logit_out, stages, device_status_ptr()); \
+  } while (0)
+        if (x_dtype == DSALT_BF16) {
+          if (x4 && v4) DSALT_SIG_BULK(DSALT_BF16, 4, 4);
+          else if (x4) DSALT_SIG_BULK(DSALT_BF16, 4, 8);
+          else if (v4) DSALT_SIG_BULK(DSALT_BF16, 8, 4);
+          else DSALT_SIG_BULK(DSALT_BF16, 8, 8);
+        } else {
+          if (x4 && v4) DSALT_SIG_BULK(DSALT_F16, 4, 4);
+          else if (x4) DSALT_SIG_BULK(DSALT_F16, 4, 8);
+          else if (v4) DSALT_SIG_BULK(DSALT_F16, 8, 4);
+          else DSALT_SIG_BULK(DSALT_F16, 8, 8);
+        }
+#undef DSALT_SIG_BULK
+        return check_cuda(cudaGetLastError(), "token_signals launch");
+      }
+    }
+    const size_t smem = (size_t)d_model * sizeof(double);
 #define DSALT_SIG_WIDE(DT, XC, VC)                                                                                 \
   token_signals_wide_kernel<DT, DT, XC, VC><<<(unsigned)blocks, threads, smem, stream>>>(                          \
       x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_stride, n_kv, head_dim, norm_mode, \
