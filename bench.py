@@ -403,28 +403,49 @@ def main():
     achieved = att_bytes / (att_ms / 1e3) / 1e9
     traffic = profiled_traffic(T)
 
-    # end to end through the C-ABI call with host buffers
+    # end to end through the C-ABI call with host buffers: every step copies its inputs in
+    # from pinned host memory and its output back, as a serving loop would: the copies run
+    # on their own streams with two device buffer sets, so that step i's output copy
+    # (device -> host) and step i+1's input copy (host -> device) overlap step i's compute
     xh = x.cpu().pin_memory()
     qh, kh, vh = q.cpu().pin_memory(), kk.cpu().pin_memory(), v.cpu().pin_memory()
     oh = torch.empty(T, H, D, dtype=torch.bfloat16).pin_memory()
-    xd, qd, kd, vd = torch.empty_like(x), torch.empty_like(q), torch.empty_like(kk), torch.empty_like(v)
+    bufs = [(torch.empty_like(x), torch.empty_like(q), torch.empty_like(kk), torch.empty_like(v),
+             torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        xd.copy_(xh, non_blocking=True)
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
+    def e2e_step(i):
+        b = i % 2
+        xd, qd, kd, vd, od = bufs[b]
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_done[b])  # step i-2's compute has read this buffer set
+            xd.copy_(xh, non_blocking=True)
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+            ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[b])  # step i-2's output has left this buffer
         ops.core_forward(xd, gw, gb, CFG["n_min"], CFG["n_max"], alpha, qd, kd, vd, k, cu_t, mode="block_causal",
-                         block=B, cu_list=cu, workspace=ws, out=out)
-        oh.copy_(out, non_blocking=True)
+                         block=B, cu_list=cu, workspace=ws, out=od)
+        ev_done[b].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_done[b])
+            oh.copy_(od, non_blocking=True)
+            ev_out[b].record(s_out)
 
-    for _ in range(2):
-        e2e_step()
+    for i in range(2):
+        e2e_step(i)
     torch.cuda.synchronize()
     barrier(world)
     e0.record(stream)
-    for _ in range(args.e2e_steps):
-        e2e_step()
+    s_in.wait_stream(stream)
+    for i in range(args.e2e_steps):
+        e2e_step(i)
+    stream.wait_stream(s_out)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
