@@ -139,3 +139,26 @@ def test_fp16_block_causal_ragged_blocks(ops):
              for i in range(len(cu) - 1)]
     np.testing.assert_array_equal(lmk.cpu().numpy(), np.concatenate(parts, axis=1))
     _check_attention(ops, q, kk, v, w, lmk.cpu(), cu, lmk_block=384, rows=np.arange(0, 1800, 4))
+
+
+@pytest.mark.parametrize("d_model,n_kv,head_dim,T", [(1024, 16, 64, 1000), (1024, 16, 64, 5003),
+                                                     (2048, 16, 128, 3001)])
+def test_signals_bulk_and_fallback_paths(ops, d_model, n_kv, head_dim, T):
+    """Widths and norms bit-exact against the oracle on both 16-bit paths: rows that fit
+    in shared memory (bulk copies, d_model 1024) and rows that do not (plain loads,
+    d_model 2048 with 16 x 128 value heads), with token counts that leave warps idle or
+    give them two tokens."""
+    g0 = torch.Generator().manual_seed(d_model + T)
+    x = torch.randn(T, d_model, generator=g0).bfloat16()
+    gw = (0.05 * torch.randn(d_model, generator=g0)).bfloat16()
+    gb = torch.tensor([0.1]).bfloat16()
+    v = torch.randn(T, n_kv * head_dim, generator=g0).bfloat16()
+    w, xn, vn, lg = ops.window_signals(x.to(_dev()), gw.to(_dev()), gb.to(_dev()), 16, 512, v.to(_dev()), head_dim,
+                                       False, return_logit=True)
+    lo = O.window_logit(x.float().numpy(), gw.float().numpy(), float(gb.float()[0]), "bf16")
+    np.testing.assert_array_equal(lg.cpu().numpy(), lo)
+    wo, amb = O.window_sizes_from_logit(lo, 16, 512, "bf16")
+    assert not ((w.cpu().numpy() != wo) & ~amb).any()
+    np.testing.assert_array_equal(xn.cpu().numpy(), O.row_norms(x.float().numpy(), None))
+    np.testing.assert_array_equal(vn.cpu().numpy(),
+                                  O.row_norms(v.float().numpy().reshape(T, n_kv, head_dim), None))
