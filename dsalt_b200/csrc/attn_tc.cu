@@ -234,6 +234,11 @@ __device__ __forceinline__ float2 up2(uint64_t r) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(r));
   return d;
 }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
@@ -798,18 +803,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_arrive(B.o_empty);
       if (vrow) {
         const bool good = l > 1e-9f;
-        const float inv = good ? 1.0f / l : 0.0f;
+        const float inv = good ? __frcp_rn(l) : 0.0f;  // = 1 / l, correctly rounded
         const int64_t row = (int64_t)f.qb + i;
         // the row's HD outputs, as 32-bit words (fp32 values or 16-bit pairs)
         const bool f32o = p.out_dtype == DSALT_F32;
-        if (f32o) {
+        const uint64_t inv2 = pk2(inv, inv);
 #pragma unroll
-          for (int d = 0; d < HD; ++d) acc[d] *= inv;
-        } else {
+        for (int d = 0; d < HD; d += 2) {
+          const float2 y = up2(mul2(pk2(acc[d], acc[d + 1]), inv2));
+          acc[d] = y.x;
+          acc[d + 1] = y.y;
+        }
+        if (!f32o) {
           const bool bo = p.out_dtype == DSALT_BF16;
 #pragma unroll
           for (int d = 0; d < HD; d += 2) {
-            const uint32_t w2 = bo ? pack_bf16x2(acc[d] * inv, acc[d + 1] * inv) : pack_f16x2(acc[d] * inv, acc[d + 1] * inv);
+            const uint32_t w2 = bo ? pack_bf16x2(acc[d], acc[d + 1]) : pack_f16x2(acc[d], acc[d + 1]);
             acc[d / 2] = __uint_as_float(w2);
           }
         }
