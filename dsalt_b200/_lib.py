@@ -30,8 +30,9 @@ SIGNATURES = {
     "dsalt_last_error": (ctypes.c_char_p, []),
     "dsalt_version": (_I, []),
     "dsalt_device_status": (_I, [ctypes.POINTER(_I), _I, _P]),
+    "dsalt_device_status_async": (_I, [_P, _P]),
     "dsalt_token_signals": (_I, [_P, _I, _I64, _I, _I64, _P, _P, _I, _I, _I, _P, _I, _I64, _I, _I, _I,
-                                 _P, _P, _P, _P, _P]),
+                                 _P, _P, _P, _P, _P, _P]),
     "dsalt_select_workspace_bytes": (_SZ, [_I, _I64, _I, _I, _I, _I, _I, _I]),
     "dsalt_select_landmarks": (_I, [_I, _P, _P, _P, _P, _P, _I, _I64, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
     "dsalt_attention_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I]),
@@ -51,7 +52,7 @@ SIGNATURES = {
     "dsalt_ipc_open": (_I, [_P, _I64, ctypes.POINTER(_P)]),
     "dsalt_ipc_close": (_I, [_P, _I64]),
     "dsalt_core_workspace_bytes": (_SZ, [_I, _I64, _I, _I, _I, _I, _I, _I, _I]),
-    "dsalt_core_forward": (_I, [_I, _P, _I, _I, _I64, _P, _P, _I, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _I,
+    "dsalt_core_forward": (_I, [_I, _P, _I, _I, _I64, _P, _P, _I, _P, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _I,
                                 _I64, _I64, _I, _I, _P, _I, _I64, _I, _P, _I, _P, _P, _P, _SZ, _P]),
 }
 

@@ -15,7 +15,7 @@ namespace dsalt {
 int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride, const void* gate_w,
                          const void* gate_b, int gate_dtype, int n_min, int n_max, const void* v, int v_dtype,
                          int64_t v_stride, int n_kv, int head_dim, int norm_mode, int32_t* w_out, float* xnorm_out,
-                         float* vnorm_out, float* logit_out, cudaStream_t stream);
+                         float* vnorm_out, float* logit_out, const void* logit_in, cudaStream_t stream);
 size_t select_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv, int k,
                               int block);
 int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
@@ -131,12 +131,21 @@ int dsalt_device_status(int* status_out, int clear, void* stream) {
   return check_cuda(cudaStreamSynchronize(s), "device_status sync");
 }
 
+int dsalt_device_status_async(int* status_host, void* stream) {
+  if (!status_host) return fail(DSALT_ERR_INVALID, "device_status_async: null output");
+  int* p = device_status_ptr();
+  if (!p) return fail(DSALT_ERR_CUDA, "device_status_async: symbol address unavailable");
+  return check_cuda(cudaMemcpyAsync(status_host, p, sizeof(int), cudaMemcpyDeviceToHost,
+                                    reinterpret_cast<cudaStream_t>(stream)),
+                    "device_status_async copy");
+}
+
 int dsalt_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride, const void* gate_w,
                         const void* gate_b, int gate_dtype, int n_min, int n_max, const void* v, int v_dtype,
                         int64_t v_stride, int n_kv, int head_dim, int norm_mode, int32_t* w_out, float* xnorm_out,
-                        float* vnorm_out, float* logit_out, void* stream) {
+                        float* vnorm_out, float* logit_out, const void* logit_in, void* stream) {
   return launch_token_signals(x, x_dtype, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_dtype,
-                              v_stride, n_kv, head_dim, norm_mode, w_out, xnorm_out, vnorm_out, logit_out,
+                              v_stride, n_kv, head_dim, norm_mode, w_out, xnorm_out, vnorm_out, logit_out, logit_in,
                               reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -361,8 +370,8 @@ size_t dsalt_core_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqle
 }
 
 int dsalt_core_forward(int mode, const void* x, int x_dtype, int d_model, int64_t x_stride, const void* gate_w,
-                       const void* gate_b, int gate_dtype, int n_min, int n_max, const float* alpha, int norm_mode,
-                       const void* q, const void* k, const void* v, int qkv_dtype, int n_heads, int n_kv,
+                       const void* gate_b, int gate_dtype, const void* logit_in, int n_min, int n_max,
+                       const float* alpha, int norm_mode, const void* q, const void* k, const void* v, int qkv_dtype, int n_heads, int n_kv,
                        int head_dim, int64_t q_stride, int64_t kv_stride, int k_lmk, int block,
                        const int32_t* cu_seqlens, int n_seqs, int64_t T, int max_seqlen, void* out, int out_dtype,
                        int32_t* w_out, int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream) {
@@ -388,7 +397,7 @@ int dsalt_core_forward(int mode, const void* x, int x_dtype, int d_model, int64_
   void* sws = ws + off;
   const size_t sws_bytes = workspace_bytes - off;
   int rc = dsalt_token_signals(x, x_dtype, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v,
-                               qkv_dtype, kv_stride, n_kv, head_dim, norm_mode, w, xn, vn, nullptr, stream);
+                               qkv_dtype, kv_stride, n_kv, head_dim, norm_mode, w, xn, vn, nullptr, logit_in, stream);
   if (rc) return rc;
   rc = dsalt_select_landmarks(mode, xn, vn, w, alpha, cu_seqlens, n_seqs, T, max_seqlen, n_heads, n_kv, k_lmk, block,
                               lmk, nullptr, nullptr, sws, sws_bytes, stream);

@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(256) token_signals_kernel(
     const void* __restrict__ x, int64_t T, int d_model, int64_t x_stride, const void* __restrict__ gate_w,
     const void* __restrict__ gate_b, int gate_dt, int n_min, int n_max, const void* __restrict__ v, int64_t v_stride,
     int n_kv, int head_dim, int norm_mode, int32_t* __restrict__ w_out, float* __restrict__ xnorm_out,
-    float* __restrict__ vnorm_out, float* __restrict__ logit_out) {
+    float* __restrict__ vnorm_out, float* __restrict__ logit_out, const void* __restrict__ logit_in) {
   constexpr int XN = Vec<XDT>::N;
   constexpr int VN = Vec<VDT>::N;
   const int lane = threadIdx.x & 31;
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(256) token_signals_kernel(
       sq += __shfl_xor_sync(0xffffffffu, sq, o);
     }
     if (lane == 0) {
-      const float logit = f64_to(dot + bias, gate_dt);
+      const float logit = logit_in ? load_elem(logit_in, t, gate_dt) : f64_to(dot + bias, gate_dt);
       w_out[t] = width_from_logit(logit, gate_dt, n_min, n_max);
       if (logit_out) logit_out[t] = logit;
       float xn = sqrtf(__double2float_rn(sq));
@@ -185,7 +185,8 @@ template <int XDT, int VDT, int XCM, int VCM>
 __device__ __forceinline__ void reduce_token(const uint4* xq, const uint4* vq, const double* gws, int lane, int xc,
                                              int vc, int vcpg, bool xg_is_x, int gate_dt, double bias, int n_min,
                                              int n_max, int norm_mode, int n_kv, int64_t t, int32_t* w_out,
-                                             float* xnorm_out, float* vnorm_out, float* logit_out) {
+                                             float* xnorm_out, float* vnorm_out, float* logit_out,
+                                             const void* logit_in) {
   constexpr int XN = Vec<XDT>::N;
   constexpr int VN = Vec<VDT>::N;
   double dot = 0.0, sq = 0.0;
@@ -195,7 +196,14 @@ __device__ __forceinline__ void reduce_token(const uint4* xq, const uint4* vq, c
       float xv[XN];
       Vec<XDT>::unpack(xq[j], xv);
       const double* gj = gws + j * XN * 32 + lane;
-      if (xg_is_x) {
+      if (logit_in) {
+        // the caller's logit: only the norm's sum
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+          const double xd = (double)xv[i];
+          sq = __fma_rn(xd, xd, sq);
+        }
+      } else if (xg_is_x) {
 #pragma unroll
         for (int i = 0; i < XN; ++i) {
           const double xd = (double)xv[i];
@@ -218,7 +226,7 @@ __device__ __forceinline__ void reduce_token(const uint4* xq, const uint4* vq, c
     sq += __shfl_xor_sync(0xffffffffu, sq, o);
   }
   if (lane == 0) {
-    const float logit = f64_to(dot + bias, gate_dt);
+    const float logit = logit_in ? load_elem(logit_in, t, gate_dt) : f64_to(dot + bias, gate_dt);
     w_out[t] = width_from_logit(logit, gate_dt, n_min, n_max);
     if (logit_out) logit_out[t] = logit;
     float xn = sqrtf(__double2float_rn(sq));
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(256) token_signals_wide_kernel(
     const void* __restrict__ x, int64_t T, int d_model, int64_t x_stride, const void* __restrict__ gate_w,
     const void* __restrict__ gate_b, int gate_dt, int n_min, int n_max, const void* __restrict__ v, int64_t v_stride,
     int n_kv, int head_dim, int norm_mode, int32_t* __restrict__ w_out, float* __restrict__ xnorm_out,
-    float* __restrict__ vnorm_out, float* __restrict__ logit_out) {
+    float* __restrict__ vnorm_out, float* __restrict__ logit_out, const void* __restrict__ logit_in) {
   constexpr int XN = Vec<XDT>::N;
   constexpr int VN = Vec<VDT>::N;
   // gate weight of element i of chunk lane + 32 j at gws[(j * XN + i) * 32 + lane]: the lanes
@@ -290,7 +298,7 @@ __global__ void __launch_bounds__(256) token_signals_wide_kernel(
       ldg16x4(vr + lane + 32 * (j < vc ? j : 0), vr + lane + 32 * (j + 1 < vc ? j + 1 : 0),
               vr + lane + 32 * (j + 2 < vc ? j + 2 : 0), vr + lane + 32 * (j + 3 < vc ? j + 3 : 0), vq + j);
     reduce_token<XDT, VDT, XCM, VCM>(xq, vq, gws, lane, xc, vc, vcpg, xg_is_x, gate_dt, bias, n_min, n_max, norm_mode,
-                                     n_kv, t, w_out, xnorm_out, vnorm_out, logit_out);
+                                     n_kv, t, w_out, xnorm_out, vnorm_out, logit_out, logit_in);
   }
 }
 
@@ -307,7 +315,8 @@ __global__ void __launch_bounds__(1024) token_signals_bulk_kernel(
     const void* __restrict__ x, int64_t T, int d_model, int64_t x_stride, const void* __restrict__ gate_w,
     const void* __restrict__ gate_b, int gate_dt, int n_min, int n_max, const void* __restrict__ v, int64_t v_stride,
     int n_kv, int head_dim, int norm_mode, int32_t* __restrict__ w_out, float* __restrict__ xnorm_out,
-    float* __restrict__ vnorm_out, float* __restrict__ logit_out, int stages, int* __restrict__ err) {
+    float* __restrict__ vnorm_out, float* __restrict__ logit_out, const void* __restrict__ logit_in, int stages,
+    int* __restrict__ err) {
   constexpr int XN = Vec<XDT>::N;
   constexpr int VN = Vec<VDT>::N;
   extern __shared__ __align__(128) unsigned char sig_smem[];
@@ -364,7 +373,7 @@ __global__ void __launch_bounds__(1024) token_signals_bulk_kernel(
       issue(t + stages * nwarps, st);
     }
     reduce_token<XDT, VDT, XCM, VCM>(xq, vq, gws, lane, xc, vc, vcpg, xg_is_x, gate_dt, bias, n_min, n_max, norm_mode,
-                                     n_kv, t, w_out, xnorm_out, vnorm_out, logit_out);
+                                     n_kv, t, w_out, xnorm_out, vnorm_out, logit_out, logit_in);
   }
 }
 
@@ -373,7 +382,7 @@ static bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
 int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride, const void* gate_w,
                          const void* gate_b, int gate_dtype, int n_min, int n_max, const void* v, int v_dtype,
                          int64_t v_stride, int n_kv, int head_dim, int norm_mode, int32_t* w_out, float* xnorm_out,
-                         float* vnorm_out, float* logit_out, cudaStream_t stream) {
+                         float* vnorm_out, float* logit_out, const void* logit_in, cudaStream_t stream) {
   if (T < 0 || d_model <= 0 || n_kv <= 0 || head_dim <= 0) return fail(DSALT_ERR_INVALID, "token_signals: bad sizes");
   if (T == 0) return DSALT_OK;
   if (!x || !gate_w || !gate_b || !v || !w_out || !xnorm_out || !vnorm_out)
@@ -421,7 +430,7 @@ int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int
       return rc;                                                                                                      \
     kern<<<(unsigned)bblocks, wpb * 32, smem_b, stream>>>(x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, \
                                                          n_max, v, v_stride, n_kv, head_dim, norm_mode, w_out,         \
-                                                         xnorm_out, vnorm_out, logit_out, stages, device_status_ptr()); \
+                                                         xnorm_out, vnorm_out, logit_out, logit_in, stages, device_status_ptr()); \
   } while (0)
         if (x_dtype == DSALT_BF16) {
           if (x4 && v4) DSALT_SIG_BULK(DSALT_BF16, 4, 4);
@@ -442,7 +451,7 @@ int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int
 #define DSALT_SIG_WIDE(DT, XC, VC)                                                                                 \
   token_signals_wide_kernel<DT, DT, XC, VC><<<(unsigned)blocks, threads, smem, stream>>>(                          \
       x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_stride, n_kv, head_dim, norm_mode, \
-      w_out, xnorm_out, vnorm_out, logit_out)
+      w_out, xnorm_out, vnorm_out, logit_out, logit_in)
     if (x_dtype == DSALT_BF16) {
       if (x4 && v4) DSALT_SIG_WIDE(DSALT_BF16, 4, 4);
       else if (x4) DSALT_SIG_WIDE(DSALT_BF16, 4, 8);
@@ -460,7 +469,7 @@ int launch_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int
 #define DSALT_SIG_LAUNCH(XD, VD)                                                                                   \
   token_signals_kernel<XD, VD><<<(unsigned)blocks, threads, 0, stream>>>(                                          \
       x, T, d_model, x_stride, gate_w, gate_b, gate_dtype, n_min, n_max, v, v_stride, n_kv, head_dim, norm_mode, \
-      w_out, xnorm_out, vnorm_out, logit_out)
+      w_out, xnorm_out, vnorm_out, logit_out, logit_in)
   if (x_dtype == DSALT_BF16 && v_dtype == DSALT_BF16) DSALT_SIG_LAUNCH(DSALT_BF16, DSALT_BF16);
   else if (x_dtype == DSALT_F16 && v_dtype == DSALT_F16) DSALT_SIG_LAUNCH(DSALT_F16, DSALT_F16);
   else if (x_dtype == DSALT_F32 && v_dtype == DSALT_F32) DSALT_SIG_LAUNCH(DSALT_F32, DSALT_F32);

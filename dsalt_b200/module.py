@@ -85,6 +85,9 @@ class DSALTAttention(nn.Module):
         return torch.sigmoid(self.alpha_w)
 
     def forward(self, x, cu_seqlens=None, max_seqlen=None, rope_cs=None, cu_list=None):
+        """Packed inference forward ``-> (out [T, d_model], aux 0)``. ``max_seqlen`` is
+        accepted for signature compatibility and not needed: the kernels derive every
+        sequence length from ``cu_seqlens`` (or ``cu_list``)."""
         if cu_seqlens is None:
             raise NotImplementedError("dsalt_b200 implements the packed path; pass cu_seqlens")
         if self.training:
@@ -108,13 +111,16 @@ class DSALTAttention(nn.Module):
         cos, sin = cos.to(q.dtype), sin.to(q.dtype)
         q, k = apply_rotary_emb(q, k, cos.unsqueeze(1), sin.unsqueeze(1))
         amp = torch.is_autocast_enabled("cuda") if x.is_cuda else False
-        gdt = torch.get_autocast_dtype("cuda") if amp else x.dtype
+        # the width logit comes from the same library op as the reference's
+        # _window_continuous (win_gate(x), :275), so that the widths equal the reference's
+        logit = self.win_gate(x).squeeze(-1)
+        gdt = logit.dtype
         gw = self.win_gate.weight.to(gdt)
         gb = self.win_gate.bias.to(gdt)
         # value norms use x·W_Vᵀ, which is the v_proj output when there is no bias
         vs = v if self.v_proj.bias is None else F.linear(x, self.v_proj.weight.to(v.dtype))
         norm_round = (x.dtype != torch.float32) and not amp
-        w, xn, vn = ops.window_signals(x, gw, gb, self.n_min, self.n_max, vs, D, norm_round)
+        w, xn, vn = ops.window_signals(x, gw, gb, self.n_min, self.n_max, vs, D, norm_round, logit=logit)
         alpha = self._alpha().detach().float()
         mode = "global" if self.selection == "global" else "block_causal"
         lmk = ops.select_landmarks(xn, vn, w, alpha, cu_seqlens, self.k_lmk, H, mode, self.block, cu_list=cu_h)

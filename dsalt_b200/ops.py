@@ -68,15 +68,22 @@ def _workspace(nbytes: int, device) -> torch.Tensor:
 
 # --------------------------------------------------------------------------- widths
 def window_signals(x, gate_weight, gate_bias, n_min: int, n_max: int, v, head_dim: int, norm_round: bool = False,
-                   return_logit: bool = False):
+                   return_logit: bool = False, logit=None):
     """Widths ``w [T] int32``, ``‖x‖ [T] fp32`` and value norms ``[T, n_kv] fp32``.
 
     ``gate_weight``/``gate_bias`` are ``win_gate``'s parameters already in the dtype the
     logit is computed in (the autocast dtype under autocast). ``v`` is ``x·W_Vᵀ``
     (``[T, n_kv·head_dim]``, or a ``[T, n_kv, head_dim]`` view). ``norm_round`` rounds the
     norms to the input dtype (a half-precision ``norm`` outside autocast).
+
+    ``logit`` (``[T]`` or ``[T, 1]`` in ``gate_weight``'s dtype) is ``win_gate(x)`` as the
+    caller computed it, e.g. by the same library GEMV the reference's
+    ``_window_continuous`` calls (``dsalt/modules/dsalt_attention.py:275``); the widths are
+    then taken from it, which makes them equal to the reference's on the same GPU. Without
+    it the kernel forms the logit itself (float64 dot product rounded once), which can
+    round to the neighbouring value of an fp32-accumulating GEMV.
     """
-    _cuda(x, gate_weight, gate_bias, v)
+    _cuda(x, gate_weight, gate_bias, v, logit)
     T, dm = x.shape
     v2 = v.reshape(T, -1)
     if v2.stride(1) != 1:
@@ -90,12 +97,25 @@ def window_signals(x, gate_weight, gate_bias, n_min: int, n_max: int, v, head_di
     xn = torch.empty(T, dtype=torch.float32, device=x.device)
     vn = torch.empty(T, n_kv, dtype=torch.float32, device=x.device)
     lg = torch.empty(T, dtype=torch.float32, device=x.device) if return_logit else None
+    lin = _logit_in(logit, T, gw.dtype)
     L.call("dsalt_token_signals", _ptr(x), _dt(x), T, dm, x.stride(0), _ptr(gw), _ptr(gb), _dt(gw), int(n_min),
            int(n_max), _ptr(v2), _dt(v2), v2.stride(0), n_kv, int(head_dim),
-           L.NORM_INPUT if norm_round else L.NORM_F32, _ptr(w), _ptr(xn), _ptr(vn), _ptr(lg), _stream())
+           L.NORM_INPUT if norm_round else L.NORM_F32, _ptr(w), _ptr(xn), _ptr(vn), _ptr(lg), _ptr(lin), _stream())
     if return_logit:
         return w, xn, vn, lg
     return w, xn, vn
+
+
+def _logit_in(logit, T, dtype):
+    """The caller's ``win_gate`` logit as a contiguous ``[T]`` tensor in the gate dtype."""
+    if logit is None:
+        return None
+    lg = logit.reshape(-1)
+    if lg.numel() != T:
+        raise ValueError(f"logit has {lg.numel()} entries for {T} tokens")
+    if lg.dtype != dtype:
+        raise TypeError(f"logit dtype {lg.dtype} differs from the gate dtype {dtype}")
+    return lg.contiguous()
 
 
 # --------------------------------------------------------------------------- selection
@@ -224,15 +244,16 @@ def dsalt_attention(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, *, lmk_
 # --------------------------------------------------------------------------- fused core
 def core_forward(x, gate_weight, gate_bias, n_min, n_max, alpha, q, k, v, k_lmk, cu_seqlens, *, mode="global",
                  block=512, norm_round=False, out_dtype=None, cu_list=None, return_aux=False, workspace=None,
-                 out=None):
+                 out=None, logit=None):
     """Widths, selection and attention in one C call (``dsalt_core_forward``).
 
     ``v`` ([T, n_kv, D]) is used both as attention values and for the value norms, so
-    it must equal ``x·W_Vᵀ`` (no ``v_proj`` bias). Returns the attention output
+    it must equal ``x·W_Vᵀ`` (no ``v_proj`` bias). ``logit`` is the optional caller-computed
+    ``win_gate`` logit of :func:`window_signals`. Returns the attention output
     ``[T, H, D]`` (``out_dtype``, default the input dtype) and, with ``return_aux``, the
     widths and landmark sets.
     """
-    _cuda(x, gate_weight, gate_bias, alpha, q, k, v, cu_seqlens)
+    _cuda(x, gate_weight, gate_bias, alpha, q, k, v, cu_seqlens, logit)
     T, H, D = q.shape
     n_kv = k.shape[1]
     cu_h = _host_cu(cu_seqlens, cu_list)
@@ -250,7 +271,8 @@ def core_forward(x, gate_weight, gate_bias, n_min, n_max, alpha, q, k, v, k_lmk,
     lmk = torch.empty(H, n_sets, k_lmk, dtype=torch.int32, device=dev) if return_aux else None
     need = L.query("dsalt_core_workspace_bytes", m, T, S, maxL, H, n_kv, D, k_lmk, block)
     ws = workspace if (workspace is not None and workspace.numel() >= need) else _workspace(need, dev)
-    L.call("dsalt_core_forward", m, _ptr(x), _dt(x), x.shape[1], x.stride(0), _ptr(gw), _ptr(gb), _dt(gw),
+    lin = _logit_in(logit, T, gw.dtype)
+    L.call("dsalt_core_forward", m, _ptr(x), _dt(x), x.shape[1], x.stride(0), _ptr(gw), _ptr(gb), _dt(gw), _ptr(lin),
            int(n_min), int(n_max), _ptr(alpha.float().contiguous()), L.NORM_INPUT if norm_round else L.NORM_F32,
            _ptr(q), _ptr(k), _ptr(v), _dt(q), H, n_kv, D, q.stride(0), k.stride(0), int(k_lmk), int(block),
            _ptr(_cu_i32(cu_seqlens)), S, T, maxL, _ptr(out), _dt(out), _ptr(w), _ptr(lmk), _ptr(ws), ws.numel(),

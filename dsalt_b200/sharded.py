@@ -125,7 +125,15 @@ class ShardedCore:
     ``exchange="peer"`` (default) moves the signals and the halo over NVLink peer memory
     between two device-side barriers (``dsalt_peer_barrier``); ``exchange="nccl"`` uses the
     NCCL collectives of :func:`gather_signals` / :func:`exchange_halo` and a closing
-    all-reduce."""
+    all-reduce.
+
+    Failure reporting: a device-side barrier that waits more than 2 s for a peer (a rank
+    that died or stalled) gives up, sets the device status word and lets the step finish;
+    that step's output, and every later one, is then invalid (stale signals or halo rows).
+    Every step queues an asynchronous read of the status word; :meth:`forward` raises
+    ``DsaltError`` (code ``ERR_DEVICE``) as soon as a completed read shows a non-zero
+    status — at the latest one call later — and :meth:`check` (or ``forward(..., check=True)``)
+    synchronises and raises for the step just queued."""
 
     def __init__(self, seq_len: int, n_heads: int, n_kv: int, head_dim: int, k_lmk: int, n_min: int, n_max: int,
                  block: int = 512, dtype=torch.bfloat16, group=None, exchange: str = "peer"):
@@ -165,6 +173,8 @@ class ShardedCore:
         self._ws_att = torch.empty(max(natt, 1), dtype=torch.uint8, device=dev)
         self._peers = []
         self._open_peers()
+        self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._status_event = None
 
     def _open_peers(self):
         """Peer pointer tables (CUDA IPC; own entries local): K / V shards, the signal
@@ -205,18 +215,36 @@ class ShardedCore:
         L_.call("dsalt_peer_barrier", ops._ptr(self._flag), ops._ptr(self._flags), self.world, self.rank,
                 self._epoch, ops._stream())
 
-    def forward(self, x, gate_weight, gate_bias, alpha, q):
+    def _raise_if_failed(self):
+        st = int(self._status_host[0])
+        if st != 0:
+            L_ = self.ops.L
+            raise L_.DsaltError(L_.ERR_DEVICE, "ShardedCore.forward",
+                                f"device status {st}: a kernel gave up a bounded wait (a peer rank stalled or "
+                                f"died); the step's output is invalid")
+
+    def check(self):
+        """Waits for the last queued step and raises if a kernel of any step so far gave up
+        a bounded wait (the device status word is not cleared)."""
+        if self._status_event is not None:
+            self._status_event.synchronize()
+            self._raise_if_failed()
+
+    def forward(self, x, gate_weight, gate_bias, alpha, q, check: bool = False):
         """``x [T_local, d_model]`` and ``q [T_local, H, D]`` of this rank's positions (``k_local`` /
         ``v_local`` already written). Returns this rank's attention output ``[T_local, H, D]``
-        and its landmark sets."""
+        and its landmark sets. Raises when an earlier step's status read has completed with a
+        non-zero status; ``check=True`` also waits for this step and checks it."""
         ops, p = self.ops, self.plan
         L = ops.L
         T = p.t_local
+        if self._status_event is not None and self._status_event.query():
+            self._raise_if_failed()
         # 1. own signals, into this rank's slice of the sequence arrays
         L.call("dsalt_token_signals", ops._ptr(x), ops._dt(x), T, x.shape[1], x.stride(0),
                ops._ptr(gate_weight), ops._ptr(gate_bias), ops._dt(gate_weight), self.n_min, self.n_max,
                ops._ptr(self.v_local), ops._dt(self.v_local), self.v_local.stride(0), self.n_kv, self.head_dim,
-               L.NORM_F32, ops._ptr(self._w), ops._ptr(self._xn), ops._ptr(self._vn), None, ops._stream())
+               L.NORM_F32, ops._ptr(self._w), ops._ptr(self._xn), ops._ptr(self._vn), None, None, ops._stream())
         w, xn, vn = self._sig
         row_bytes = self.k_local.stride(0) * self.k_local.element_size()
         if self.exchange == "peer":
@@ -244,4 +272,11 @@ class ShardedCore:
             self._barrier()
         else:
             dist.all_reduce(self._flag[:1], group=self.group)
+        # the device status word, read without stalling the stream
+        L.call("dsalt_device_status_async", self._status_host.data_ptr(), ops._stream())
+        if self._status_event is None:
+            self._status_event = torch.cuda.Event()
+        self._status_event.record()
+        if check:
+            self.check()
         return self.out, lmk

@@ -46,6 +46,11 @@ int dsalt_version(void);
 /* Reads (and clears, when `clear` != 0) the device status word that kernels set when a
  * bounded wait gives up. Synchronises `stream`. 0 = no error. */
 int dsalt_device_status(int* status_out, int clear, void* stream);
+/* Queues a copy of the device status word into host memory `status_host` (page-locked, so
+ * that the copy is asynchronous) on `stream` and returns without synchronising; the value
+ * is there once the stream has passed this point (e.g. an event recorded after the call
+ * has completed). Lets a caller check every step without stalling the stream. */
+int dsalt_device_status_async(int* status_host, void* stream);
 
 /*
  * Window widths and selection signals, one pass over x and v.
@@ -60,11 +65,18 @@ int dsalt_device_status(int* status_out, int clear, void* stream);
  * v        [T, n_kv*head_dim] value projection x·W_Vᵀ (row stride v_stride), dtype v_dtype
  * w_out    [T] int32 widths, xnorm_out [T] fp32, vnorm_out [T, n_kv] fp32
  * logit_out [T] fp32 (nullable): the rounded win_gate logit
+ * logit_in  [T] in gate_dtype (nullable): the win_gate logit as the caller computed it
+ *          (e.g. torch's `win_gate(x)` under autocast, the reference's own op); the widths
+ *          are then computed from it (gate_w / gate_b are still passed but no longer
+ *          affect any output). Without it the logit is the float64-accumulated dot
+ *          product rounded once to gate_dtype, which a library GEMV that accumulates in
+ *          fp32 can round to the neighbouring value.
  */
 int dsalt_token_signals(const void* x, int x_dtype, int64_t T, int d_model, int64_t x_stride,
                         const void* gate_w, const void* gate_b, int gate_dtype, int n_min, int n_max,
                         const void* v, int v_dtype, int64_t v_stride, int n_kv, int head_dim, int norm_mode,
-                        int32_t* w_out, float* xnorm_out, float* vnorm_out, float* logit_out, void* stream);
+                        int32_t* w_out, float* xnorm_out, float* vnorm_out, float* logit_out,
+                        const void* logit_in, void* stream);
 
 /*
  * Landmark selection.
@@ -201,13 +213,13 @@ int dsalt_attention_fwd_noalloc(const void* q, const void* k, const void* v, int
  * (dsalt/modules/dsalt_attention.py:610-625): widths, signals, selection, attention.
  * Scratch for the intermediates comes from `workspace`
  * (dsalt_core_workspace_bytes); w_out / lmk_out (nullable) receive copies of the widths
- * and landmark sets.
+ * and landmark sets; logit_in (nullable) is dsalt_token_signals' caller-computed logit.
  */
 size_t dsalt_core_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv,
                                   int head_dim, int k, int block);
 int dsalt_core_forward(int mode, const void* x, int x_dtype, int d_model, int64_t x_stride, const void* gate_w,
-                       const void* gate_b, int gate_dtype, int n_min, int n_max, const float* alpha,
-                       int norm_mode, const void* q, const void* k, const void* v, int qkv_dtype, int n_heads,
+                       const void* gate_b, int gate_dtype, const void* logit_in, int n_min, int n_max,
+                       const float* alpha, int norm_mode, const void* q, const void* k, const void* v, int qkv_dtype, int n_heads,
                        int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, int k_lmk, int block,
                        const int32_t* cu_seqlens, int n_seqs, int64_t T, int max_seqlen, void* out, int out_dtype,
                        int32_t* w_out, int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream);

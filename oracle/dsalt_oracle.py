@@ -428,7 +428,7 @@ def select_block_causal(xn, vn, alpha, w, L, k_lmk, n_heads, block=512, return_s
 #      causal_landmark_check.py:119-147
 # --------------------------------------------------------------------------- #
 def attention_forward(q, k, v, w, lmk, cu_seqlens, lmk_block=0, lmk_bias=None,
-                      scale=None, rows=None):
+                      scale=None, rows=None, return_mag=False):
     """Reference semantics of the inference kernel, evaluated in float64.
 
     For query ``i`` (position within its sequence) and head ``h`` the keys are the
@@ -440,7 +440,11 @@ def attention_forward(q, k, v, w, lmk, cu_seqlens, lmk_block=0, lmk_bias=None,
     ``lmk`` is ``[H, S, k]`` (``lmk_block == 0``) or ``[H, n_sets, k]`` with one set per
     ``lmk_block`` queries of each sequence, numbered sequence after sequence.
     ``rows`` optionally restricts the evaluation to a subset of packed rows.
-    Returns ``(out [T,H,D] float64 (rows not evaluated are 0), lse [T,H])``.
+    Returns ``(out [T,H,D] float64 (rows not evaluated are 0), lse [T,H])``, and with
+    ``return_mag`` also ``mag [T,H,D] = Σ_j p_j·|v_jd| / Σ_j p_j``: rounding every
+    probability to bf16 before the P·V product (the reference's
+    ``tl.dot(p.to(bf16), v)``, ``dsalt_triton_attn.py:116,148``) moves an output by at most
+    ``2^-9 · mag`` (bf16 round-to-nearest has relative error ≤ 2^-9).
     """
     q = np.asarray(q, dtype=F64)
     k = np.asarray(k, dtype=F64)
@@ -452,6 +456,7 @@ def attention_forward(q, k, v, w, lmk, cu_seqlens, lmk_block=0, lmk_bias=None,
     w = np.maximum(np.asarray(w, dtype=np.int64), 1)
     out = np.zeros((T, H, D), dtype=F64)
     lse = np.full((T, H), -np.inf, dtype=F64)
+    mag = np.zeros((T, H, D), dtype=F64) if return_mag else None
     S = len(cu_seqlens) - 1
     want = None if rows is None else np.zeros(T, dtype=bool)
     if want is not None:
@@ -488,7 +493,11 @@ def attention_forward(q, k, v, w, lmk, cu_seqlens, lmk_block=0, lmk_bias=None,
                 if l > 1e-9:
                     out[t, h] = (p @ allv) / l
                     lse[t, h] = m + math.log(l)
+                    if mag is not None:
+                        mag[t, h] = (p @ np.abs(allv)) / l
         set_base += nsets
+    if return_mag:
+        return out, lse, mag
     return out, lse
 
 

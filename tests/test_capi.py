@@ -53,7 +53,7 @@ def test_invalid_arguments_are_rejected(lib):
                                  None, 1, 0, None, L.BF16, None, None, 0, None)
     assert rc == L.ERR_INVALID
     rc = lib.dsalt_token_signals(None, 9, 8, 64, 64, None, None, L.BF16, 16, 128, None, L.BF16, 64, 1, 64, 0,
-                                 None, None, None, None, None)
+                                 None, None, None, None, None, None)
     assert rc == L.ERR_INVALID
     rc = lib.dsalt_select_landmarks(5, None, None, None, None, None, 1, 8, 8, 1, 1, 4, 0, None, None, None, None, 0,
                                     None)

@@ -16,8 +16,12 @@ def test_barrier_wait_runs_out_and_reports():
     never_set = torch.zeros(4, dtype=torch.int32, device=dev)  # the "peer": nothing writes it
     table = torch.tensor([own.data_ptr(), never_set.data_ptr()], dtype=torch.int64, device=dev)
     L.call("dsalt_peer_barrier", own.data_ptr(), table.data_ptr(), 2, 0, 1, torch.cuda.current_stream().cuda_stream)
+    # the asynchronous read (what ShardedCore queues after every step) sees the code too
+    host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    L.call("dsalt_device_status_async", host.data_ptr(), torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert int(own[0]) == 1          # this rank published its epoch
+    assert int(host[0]) == 60
     assert ops.device_status() == 60  # and gave up waiting for the peer
     # the context still works
     x = torch.arange(1024, device=dev, dtype=torch.float32)
