@@ -50,12 +50,16 @@ constexpr int NTHREADS = 384;
 // warp of each warpgroup) holds 88 + 2 x 208 = 504 <= 512 registers per lane. Each
 // setmaxnreg sits at the top of its role's branch so that the compiler allocates each
 // role with its own budget.
-constexpr uint32_t REGS_CTRL = 88, REGS_SOFTMAX = 208;
+#ifndef DSALT_REGS_CTRL
+#define DSALT_REGS_CTRL 88
+#define DSALT_REGS_SOFTMAX 208
+#endif
+constexpr uint32_t REGS_CTRL = DSALT_REGS_CTRL, REGS_SOFTMAX = DSALT_REGS_SOFTMAX;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t PIPE_COLS = 256;                 // S 128 | P 64 | O 64
 constexpr uint32_t COL_S = 0, COL_P = 128, COL_O = 192;
 constexpr int MAX_LMK = 256;
-constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P entries stay below 2^8 between rescales
+constexpr float OVERFLOW_SUM = 32768.0f;  // a tile's row sum above 2^15 (or NaN/inf) redoes the tile
 
 struct Params {
   const void* k;
@@ -268,6 +272,66 @@ __device__ __forceinline__ void mask_chunk(float* xc, float c0f, float A1, float
   }
 }
 
+// 2^y for a pair of values on the FMA pipe (the MUFU unit that runs ex2.approx issues 16
+// results per clock per SM, a quarter of the FMA pipe's rate, so a share of each chunk's
+// exponentials is computed here). Cody-Waite style reduction y = j + f with j = rint(y),
+// taken exactly by the 1.5*2^23 shift (|y| < 2^22), and |f| <= 1/2; 2^f by a degree-3
+// polynomial fitted for minimal relative error on [-1/2, 1/2] by iteratively reweighted
+// least squares (Lawson's algorithm): max relative error 7.5e-5 evaluated in fp32, well
+// below the 2^-9 of the bf16 rounding P goes through. j is added to the exponent field.
+// y is clamped to [-126, 64] first: below, the result is a value <= 2^-126 instead of
+// ~0 (the masked columns: negligible against the row's maximum, ~1); above, it is >= 2^64,
+// which the tile-sum overflow check sends to the slow path like an infinite ex2 result.
+constexpr float EXP2_C0 = 0.9999280571937561f, EXP2_C1 = 0.6932609677314758f, EXP2_C2 = 0.24261093139648438f,
+                EXP2_C3 = 0.05517149344086647f;
+constexpr float RINT_SHIFT = 12582912.0f;  // 1.5 * 2^23
+__device__ __forceinline__ void exp2_poly2(uint64_t y, float& r0, float& r1) {
+  float2 v = up2(y);
+  v.x = fminf(fmaxf(v.x, -126.0f), 64.0f);
+  v.y = fminf(fmaxf(v.y, -126.0f), 64.0f);
+  const uint64_t yc = pk2(v.x, v.y);
+  const uint64_t t = add2(yc, pk2(RINT_SHIFT, RINT_SHIFT));       // 1.5*2^23 + rint(y)
+  const uint64_t j = add2(t, pk2(-RINT_SHIFT, -RINT_SHIFT));      // rint(y)
+  const uint64_t f = fma2(j, pk2(-1.0f, -1.0f), yc);              // y - rint(y), exact
+  uint64_t q = fma2(pk2(EXP2_C3, EXP2_C3), f, pk2(EXP2_C2, EXP2_C2));
+  q = fma2(q, f, pk2(EXP2_C1, EXP2_C1));
+  q = fma2(q, f, pk2(EXP2_C0, EXP2_C0));
+  const float2 qq = up2(q), tt = up2(t);
+  // the low 9 bits of t's encoding hold rint(y) mod 512: shifted by 23 they add rint(y) to
+  // the exponent of 2^f (in [2^-1/2, 2^1/2]; exponent >= 126 - 126 stays non-negative)
+  r0 = __uint_as_float(__float_as_uint(qq.x) + (__float_as_uint(tt.x) << 23));
+  r1 = __uint_as_float(__float_as_uint(qq.y) + (__float_as_uint(tt.y) << 23));
+}
+
+// Pairs of a 32-column chunk whose exponentials take the polynomial (bit i: columns 2i,
+// 2i+1); the others use ex2.approx. Measured on B200 at L = 131072 the softmax is bound by
+// latency, not by the MUFU rate, and the extra FMA-pipe instructions cost more than they
+// save (six pairs: 0.958 ms against 0.896 ms for none), so no pair uses it by default.
+#ifndef DSALT_POLY_PAIRS
+#define DSALT_POLY_PAIRS 0u
+#endif
+
+// P = 2^(x*sl - mu) of one 32-column chunk: 16-bit pairs into pk, fp32 row sums into s0/s1
+template <bool BF>
+__device__ __forceinline__ void exp_chunk(const float* xc, uint64_t sl2, uint64_t nmu2, uint64_t& s0, uint64_t& s1,
+                                          uint32_t* pk) {
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    const uint64_t y = fma2(pk2(xc[e], xc[e + 1]), sl2, nmu2);
+    float q0, q1;
+    if ((DSALT_POLY_PAIRS >> (e >> 1)) & 1u) {
+      exp2_poly2(y, q0, q1);
+    } else {
+      const float2 yy = up2(y);
+      q0 = ex2_approx(yy.x);
+      q1 = ex2_approx(yy.y);
+    }
+    if ((e >> 1) & 1) s1 = add2(s1, pk2(q0, q1));
+    else s0 = add2(s0, pk2(q0, q1));
+    pk[e >> 1] = BF ? pack_bf16x2(q0, q1) : pack_f16x2(q0, q1);
+  }
+}
+
 // 32-byte store (sm_100); the address must be 32-byte aligned
 __device__ __forceinline__ void st_global_v8(void* ptr, const uint32_t* r) {
   asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(__cvta_generic_to_global(ptr)),
@@ -372,6 +436,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
+        tma_prefetch_desc(&tm_lk);
+        tma_prefetch_desc(&tm_lv);
       }
       const uint16_t* kg = reinterpret_cast<const uint16_t*>(p.k);
       const uint16_t* vg = reinterpret_cast<const uint16_t*>(p.v);
@@ -474,36 +540,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               }
               continue;
             }
-            // landmark rows (replaces _build_landmark_kv): 16-byte cp.async by all lanes into
-            // the swizzled tiles, four rows per instruction; empty slots are zero-filled
-            // (their columns are masked by the row's landmark count, and zeros keep P·V
-            // finite). The positions come from this item's slot.
+            // landmark rows (replaces _build_landmark_kv): TMA gathers of four rows each (2-D
+            // maps over the K / V rows, one 64-column box per row, no multicast), lane l
+            // fetching rows 4l..4l+3 of the tile, so the producer never waits for them. Slots
+            // past the set's length, with position -1 or outside the sequence read the
+            // sequence's first row instead: their columns are masked by the row's landmark
+            // count and carry P = 0 (or <= 2^-126), so the values never count. The positions
+            // come from this item's slot.
             if (!mbar_wait(&B.it_full[sl_i], (uint32_t)(it / NIS) & 1, p.err, 15)) { ok = false; break; }
             if (!mbar_wait(&B.k_empty[sk], ((uint32_t)(g / NSK) & 1) ^ 1, p.err, 12)) { ok = false; break; }
             if (!mbar_wait(&B.v_empty[sv], ((uint32_t)(g / NSV) & 1) ^ 1, p.err, 14)) { ok = false; break; }
-            constexpr int CPR = HD / 8;     // 16-byte chunks per row
-            constexpr int RPI = 32 / CPR;   // rows per instruction
-            const int c = lane % CPR, rsub = lane / CPR;
-            const int64_t head_off = (int64_t)f.hk * HD + c * 8;
-            for (int rb = 0; rb < BN; rb += 32) {
-#pragma unroll
-              for (int j = 0; j < 32 / RPI; ++j) {
-                const int rr = j * RPI + rsub;
-                const int idx = lt * BN + rb + rr;
-                const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
-                const int64_t off = ((int64_t)f.kvb + (pos < 0 ? 0 : pos)) * p.kv_stride + head_off;
-                const uint32_t so = swz_off<HD>(rb + rr, c);
-                const uint32_t nb = pos < 0 ? 0u : 16u;
-                cp_async_16(kdst + so, kg + off, nb);
-                cp_async_16(vdst + so, vg + off, nb);
-              }
-            }
-            cp_async_wait_all();
-            fence_proxy_async_smem();  // generic-proxy writes -> tensor-core (async proxy) reads
-            __syncwarp();
             if (lane == 0) {
-              mbar_arrive(&B.k_full[sk]);
-              mbar_arrive(&B.v_full[sv]);
+              mbar_arrive_expect_tx(&B.k_full[sk], SM::TILE_BYTES);
+              mbar_arrive_expect_tx(&B.v_full[sv], SM::TILE_BYTES);
+            }
+            __syncwarp();
+            int rows[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int idx = lt * BN + 4 * lane + j;
+              const int pos = idx < p.k_lmk ? S.pos[idx] : -1;
+              rows[j] = f.kvb + ((unsigned)pos < (unsigned)f.L ? pos : 0);
+            }
+#pragma unroll
+            for (int a = 0; a < SM::NA; ++a) {
+              const uint32_t off = a * BM * 128 + lane * 512;
+              const int col = f.hk * HD + a * 64;
+              tma_gather4(kdst + off, &tm_lk, &B.k_full[sk], col, rows[0], rows[1], rows[2], rows[3]);
+              tma_gather4(vdst + off, &tm_lv, &B.v_full[sv], col, rows[0], rows[1], rows[2], rows[3]);
             }
           }
         }
@@ -579,7 +643,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const uint32_t tP = tpipe + lane_off + COL_P;
     const uint32_t tO = tpipe + lane_off + COL_O;
     const float sl = p.scale_log2;
-    constexpr bool bf = BF;
     uint32_t u = 0;
     bool ok = true;
     int it = 0;
@@ -610,7 +673,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_arrive(&B.it_empty[sl_i]);
       const int NK = f.nwt + f.nlt;
       const float* Bset = p.lmk_bias ? p.lmk_bias + ((int64_t)f.h * f.n_sets + f.set) * p.k_lmk : nullptr;
-      float m_acc = -INFINITY, l = 0.0f;  // running max (log2 units, stale by at most 2^8) and row sum
+      float m_acc = -INFINITY, l = 0.0f;  // running max (log2 units, stale) and row sum
       for (int t = 0; t < NK; ++t) {
         if (!mbar_wait(B.s_full, u & 1, p.err, 32)) { ok = false; break; }
         tc_fence_after();
@@ -645,12 +708,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const float A1 = MASK_C * (0.5f - (float)a), A2 = MASK_C * ((float)b + 0.5f);
         uint64_t s0 = pk2(0.f, 0.f), s1 = s0;
-        // Fast path (every tile after the first): exponentials against the running max,
-        // chunk by chunk, P stored to TMEM per chunk once the previous P·V has released the
-        // P buffer. A chunk whose maximum exceeds the running max by more than the rescale
-        // threshold in any lane sends the warp to the slow path, which redoes the tile.
-        // Per 32-column chunk the warp masks only when some lane keeps part of it, and
-        // skips the exponentials when no lane keeps any of it.
         // chunk classes, warp-uniform: bit c of `none` = no lane keeps chunk c (skipped);
         // bit c of `all` = every lane keeps all of chunk c (no masking)
         uint32_t none_l = 0, all_l = 0;
@@ -662,45 +719,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t none = __reduce_and_sync(0xffffffffu, none_l), all = __reduce_and_sync(0xffffffffu, all_l);
         bool slow = t == 0, p_free = t == 0;
         if (!slow) {
-          // exponentials against the running max; the chunk maxima are checked once, after
-          // the tile (a rare overflow redoes the tile on the slow path)
+          // Fast path (every tile after the first): exponentials against the running max,
+          // chunk by chunk, P stored to TMEM per chunk once the previous P·V has released the
+          // P buffer. Overflow check on the tile's row sum: while it stays below 2^15 no P
+          // entry exceeds 2^15 (finite in fp16 and bf16); otherwise the tile is redone on the
+          // slow path with the row's new maximum.
           const float mu = (m_acc == -INFINITY) ? 0.0f : m_acc;
           const uint64_t sl2 = pk2(sl, sl), nmu2 = pk2(-mu, -mu);
-          float cm = -INFINITY;
-          uint32_t pk0[16];  // chunk 0's P, stored with chunk 1's (the previous P·V has more time)
 #pragma unroll
           for (int cc = 0; cc < BN / 32; ++cc) {
-            const int c0 = cc * 32;
             uint32_t pk[16];
             if ((none >> cc) & 1) {
 #pragma unroll
               for (int e = 0; e < 16; ++e) pk[e] = 0u;
             } else {
-              float* xc = x + c0;
-              if (!((all >> cc) & 1)) mask_chunk(xc, (float)c0, A1, A2);
-              float c0m = fmax3f(xc[0], xc[1], xc[2]), c1m = fmax3f(xc[3], xc[4], xc[5]);
-#pragma unroll
-              for (int e = 6; e < 30; e += 4) {
-                c0m = fmax3f(c0m, xc[e], xc[e + 1]);
-                c1m = fmax3f(c1m, xc[e + 2], xc[e + 3]);
-              }
-              cm = fmax3f(cm, c0m, fmax3f(c1m, xc[30], xc[31]));
-#pragma unroll
-              for (int e = 0; e < 32; e += 4) {
-                const float2 y0 = up2(fma2(pk2(xc[e], xc[e + 1]), sl2, nmu2));
-                const float2 y1 = up2(fma2(pk2(xc[e + 2], xc[e + 3]), sl2, nmu2));
-                const float p0 = ex2_approx(y0.x), p1 = ex2_approx(y0.y);
-                const float p2 = ex2_approx(y1.x), p3 = ex2_approx(y1.y);
-                s0 = add2(s0, pk2(p0, p1));
-                s1 = add2(s1, pk2(p2, p3));
-                pk[e >> 1] = pack_p(bf, p0, p1);
-                pk[(e >> 1) + 1] = pack_p(bf, p2, p3);
-              }
-            }
-            if (cc == 0) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) pk0[e] = pk[e];
-              continue;
+              float* xc = x + cc * 32;
+              if (!((all >> cc) & 1)) mask_chunk(xc, (float)(cc * 32), A1, A2);
+              exp_chunk<BF>(xc, sl2, nmu2, s0, s1, pk);
             }
             if (!p_free) {
               // previous P·V done: the P buffer may be overwritten
@@ -708,22 +743,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               tc_fence_after();
               p_free = true;
             }
-            if (cc == 1) DSALT_TMEM_ST16(tP, pk0);
             DSALT_TMEM_ST16(tP + cc * 16, pk);
           }
           if (!ok) break;
-          // masked-out columns hold -2^99-scaled values, so cm bounds the kept ones
-          slow = __any_sync(0xffffffffu, cm * sl > m_acc + RESCALE_THRESHOLD && a <= b);
+          const float2 ss = up2(add2(s0, s1));
+          slow = __any_sync(0xffffffffu, !(ss.x + ss.y <= OVERFLOW_SUM));
         }
         if (slow) {
-          // masked row max; O and the row sum are rescaled when it grows
+          // masked row max; O and the row sum are rescaled when it grows (a chunk masked on
+          // the fast path is masked again: min with the same thresholds changes nothing)
           float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
           for (int cc = 0; cc < BN / 32; ++cc) {
-            const int c0 = cc * 32;
             if ((none >> cc) & 1) continue;
-            float* xc = x + c0;
-            if (!((all >> cc) & 1)) mask_chunk(xc, (float)c0, A1, A2);
+            float* xc = x + cc * 32;
+            if (!((all >> cc) & 1)) mask_chunk(xc, (float)(cc * 32), A1, A2);
 #pragma unroll
             for (int e = 0; e < 32; e += 4) {
               m0 = fmax3f(m0, xc[e], xc[e + 1]);
@@ -759,24 +793,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           s1 = s0;
 #pragma unroll
           for (int cc = 0; cc < BN / 32; ++cc) {
-            const int c0 = cc * 32;
             uint32_t pk[16];
             if ((none >> cc) & 1) {
 #pragma unroll
               for (int e = 0; e < 16; ++e) pk[e] = 0u;
             } else {
-              const float* xc = x + c0;  // masked above where needed
-#pragma unroll
-              for (int e = 0; e < 32; e += 4) {
-                const float2 y0 = up2(fma2(pk2(xc[e], xc[e + 1]), sl2, nmu2));
-                const float2 y1 = up2(fma2(pk2(xc[e + 2], xc[e + 3]), sl2, nmu2));
-                const float p0 = ex2_approx(y0.x), p1 = ex2_approx(y0.y);
-                const float p2 = ex2_approx(y1.x), p3 = ex2_approx(y1.y);
-                s0 = add2(s0, pk2(p0, p1));
-                s1 = add2(s1, pk2(p2, p3));
-                pk[e >> 1] = pack_p(bf, p0, p1);
-                pk[(e >> 1) + 1] = pack_p(bf, p2, p3);
-              }
+              exp_chunk<BF>(x + cc * 32, sl2, nmu2, s0, s1, pk);  // masked above where needed
             }
             DSALT_TMEM_ST16(tP + cc * 16, pk);
           }
@@ -911,6 +933,23 @@ static int make_map(CUtensorMap* m, const void* base, int dtype, int HD, int hea
   return DSALT_OK;
 }
 
+// 2-D map over token rows of `cols` 16-bit elements (row stride row_stride elements), boxes of
+// one row x 64 columns, 128-byte swizzle: the landmark gathers (tile::gather4)
+static int make_gather_map(CUtensorMap* m, const void* base, int dtype, int64_t cols, int64_t rows,
+                           int64_t row_stride) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return fail(DSALT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  const cuuint32_t box[2] = {64, 1};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dtype == DSALT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DSALT_ERR_CUDA, "cuTensorMapEncodeTiled (gather) failed (%d)", (int)r);
+  return DSALT_OK;
+}
+
 }  // namespace tc
 
 int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int HD,
@@ -960,7 +999,16 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   p.set_base = set_base;
   p.tile_base = tile_base;
   p.plan = plan;
-  CUtensorMap mlk = mk, mlv = mv;
+  CUtensorMap mlk, mlv;
+  if (!shard) {
+    // landmark rows: 2-D maps (rows = tokens, columns = all kv heads), one-row boxes, for
+    // the four-row TMA gathers
+    if ((rc = make_gather_map(&mlk, k, dtype, (int64_t)Hkv * HD, T, kv_stride))) return rc;
+    if ((rc = make_gather_map(&mlv, v, dtype, (int64_t)Hkv * HD, T, kv_stride))) return rc;
+  } else {
+    mlk = mk;
+    mlv = mv;
+  }
   if (shard) {
     p.shard_tiles = shard_tiles;
     p.n_sets_local = lmk_block ? (int)((shard->q_rows + lmk_block - 1) / lmk_block) : 1;

@@ -236,6 +236,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t smem_addr, const void* tmap
       "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// TMA gather of four rows of a 2-D tensor map (box: one row of 64 columns) into four
+// consecutive 128-byte rows of shared memory, completion on an mbarrier (no multicast).
+// col: first column (a multiple of 8 for 16-bit data); r0..r3: row coordinates.
+__device__ __forceinline__ void tma_gather4(uint32_t smem_addr, const void* tmap, uint64_t* bar, int col, int r0,
+                                            int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6, %7}], [%2];" ::"r"(smem_addr),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

@@ -444,7 +444,7 @@ def attention_forward(q, k, v, w, lmk, cu_seqlens, lmk_block=0, lmk_bias=None,
     ``return_mag`` also ``mag [T,H,D] = Σ_j p_j·|v_jd| / Σ_j p_j``: rounding every
     probability to bf16 before the P·V product (the reference's
     ``tl.dot(p.to(bf16), v)``, ``dsalt_triton_attn.py:116,148``) moves an output by at most
-    ``2^-9 · mag`` (bf16 round-to-nearest has relative error ≤ 2^-9).
+    ``2^-8 · mag`` (bf16 keeps 8 significant bits: round-to-nearest relative error ≤ 2^-8).
     """
     q = np.asarray(q, dtype=F64)
     k = np.asarray(k, dtype=F64)

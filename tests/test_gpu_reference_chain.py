@@ -13,10 +13,12 @@
 
 Attention tolerance. The reference multiplies bf16-rounded probabilities with V
 (``tl.dot(p.to(bf16), v)``, ``dsalt/kernels/dsalt_triton_attn.py:116,148``), so its
-output differs from exact softmax attention by up to ``2^-9 · Σ p|v| / Σ p`` per element
-(bf16 round-to-nearest: relative error ≤ 2^-9). The kernel computes the same product; its
-error against the fp64 oracle must stay within that bound plus 1e-4 for the fp32
-accumulations, and the max-abs error is printed beside the north-star 2e-3.
+output differs from exact softmax attention by up to ``2^-8 · Σ p|v| / Σ p`` per element
+(bf16 keeps 8 significant bits: round-to-nearest has relative error ≤ 2^-8). The kernel
+computes the same product, with part of its exponentials from a polynomial of relative
+error ≤ 7.5e-5; its error against the fp64 oracle must stay within
+``(2^-8 + 2^-12) · Σ p|v| / Σ p + 1e-4`` (the last term for the fp32 accumulations), and
+the max-abs error is printed beside the north-star 2e-3.
 """
 import numpy as np
 import pytest
@@ -143,7 +145,7 @@ def test_cfg2_full_shape_parity(ops):
     ref, _, mag = O.attention_forward(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
                                       wn, lo, cu, rows=rows, return_mag=True)
     err = np.abs(out.cpu().numpy()[rows] - ref[rows])
-    bound = 2.0 ** -9 * mag[rows] + ACC_TOL
+    bound = (2.0 ** -8 + 2.0 ** -12) * mag[rows] + ACC_TOL
     print(f"\ncfg2 full shape: max |out - exact| = {err.max():.2e} over {err.size} values "
           f"({int((err > 2e-3).sum())} above 2e-3); max err / bf16-P bound = {(err / bound).max():.3f}")
     assert (err <= bound).all(), float((err / bound).max())
