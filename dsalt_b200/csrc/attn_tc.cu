@@ -256,19 +256,15 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
 
 // Masks the 32 columns c0 + e of a chunk outside the row's valid range [a, b]:
 // x = min(x, t1, t2) with the exact thresholds t1(c) = C(c − a + ½) = C·c + A1 and
-// t2(c) = C(b + ½ − c) = −C·c + A2, stepped two columns at a time by packed adds of ±2C
-// (exact: the thresholds stay half-integers times 2^100)
+// t2(c) = C(b + ½ − c) = A2 − C·c. C·c is a compile-time constant (c0 is), so each threshold
+// is one exact fp32 add (half-integers times 2^100 stay exact below 2^24), and the 32
+// columns have no dependency chain between them (stepping the thresholds by packed adds,
+// two columns at a time, made a 16-long chain that cost more than the adds it saved).
 __device__ __forceinline__ void mask_chunk(float* xc, float c0f, float A1, float A2) {
-  uint64_t t1 = pk2(fmaf(MASK_C, c0f, A1), fmaf(MASK_C, c0f + 1.0f, A1));
-  uint64_t t2 = pk2(fmaf(-MASK_C, c0f, A2), fmaf(-MASK_C, c0f + 1.0f, A2));
-  const uint64_t d1 = pk2(2.0f * MASK_C, 2.0f * MASK_C), d2 = pk2(-2.0f * MASK_C, -2.0f * MASK_C);
 #pragma unroll
-  for (int e = 0; e < 32; e += 2) {
-    const float2 u1 = up2(t1), u2 = up2(t2);
-    xc[e] = fmin3f(xc[e], u1.x, u2.x);
-    xc[e + 1] = fmin3f(xc[e + 1], u1.y, u2.y);
-    t1 = add2(t1, d1);
-    t2 = add2(t2, d2);
+  for (int e = 0; e < 32; ++e) {
+    const float k = MASK_C * (c0f + (float)e);
+    xc[e] = fmin3f(xc[e], A1 + k, A2 - k);
   }
 }
 
@@ -825,7 +821,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_arrive(B.o_empty);
       if (vrow) {
         const bool good = l > 1e-9f;
-        const float inv = good ? __frcp_rn(l) : 0.0f;  // = 1 / l, correctly rounded
+        float inv = 0.0f;  // 1 / l (MUFU approximation, ~1 ulp: far below the output rounding)
+        if (good) asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(l));
         const int64_t row = (int64_t)f.qb + i;
         // the row's HD outputs, as 32-bit words (fp32 values or 16-bit pairs)
         const bool f32o = p.out_dtype == DSALT_F32;
