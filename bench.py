@@ -81,41 +81,61 @@ def make_inputs(dev, seed=0):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle samples taken during the timed region."""
+    """nvidia-smi clock / throttle samples taken during the timed region: a reader thread
+    collects one line per 10 ms; entering waits (up to 3 s) for the first sample, so that
+    sampling is running before the timed region starts, and leaving takes one more."""
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
+
+    def _reader(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.lines.append(ln)
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index),
                  "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                  "clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "10"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._reader, daemon=True)
+        self.thread.start()
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
+            time.sleep(0.005)
+        self.n0 = len(self.lines)
         return self
 
     def __exit__(self, *a):
-        self.lines = []
         if self.proc is not None:
+            n = len(self.lines)
+            t0 = time.time()
+            while len(self.lines) <= n and time.time() - t0 < 0.5 and self.proc.poll() is None:
+                time.sleep(0.002)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out = ""
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self.thread.join(timeout=2)
         return False
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        # the samples from the last one before the timed region to the first one after it
+        lines = self.lines[max(getattr(self, "n0", 1) - 1, 0):]
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 7:
                 continue

@@ -43,6 +43,8 @@ SIGNATURES = {
     "dsalt_select_block_range_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I]),
     "dsalt_select_block_range": (_I, [_P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _I, _P, _P, _SZ, _P]),
     "dsalt_attention_sharded_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I]),
+    "dsalt_select_shard_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I]),
+    "dsalt_select_shard": (_I, [_I, _P, _P, _P, _P, _I64, _I, _I, _I, _I, _I, _I, _P, _SZ, _P, _P, _P]),
     "dsalt_attention_fwd_sharded": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _I64, _I64, _I64, _I64,
                                          _P, _P, _P, _I, _I, _P, _P, _I64, _P, _I, _P, _P, _SZ, _P]),
     "dsalt_peer_barrier": (_I, [_P, _P, _I, _I, _I, _P]),

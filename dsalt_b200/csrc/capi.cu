@@ -27,6 +27,10 @@ int launch_select_range(const float* xnorm, const float* vnorm, const int32_t* w
                         int n_heads, int n_kv, int k, int block, int set_lo, int set_hi, int32_t* lmk_out,
                         void* workspace, size_t ws_bytes, cudaStream_t stream);
 int select_set_up_attributes();
+size_t select_shard_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block);
+int launch_select_shard(int phase, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                        int64_t seq_len, int n_heads, int n_kv, int k, int block, int rank, int n_ranks, void* workspace,
+                        size_t ws_bytes, const void* const* ws_peers, int32_t* lmk_out, cudaStream_t stream);
 int launch_attn_f32(const float* q, const float* k, const float* v, int64_t T, int H, int Hkv, int D,
                     int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                     int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, const int32_t* set_base, float scale,
@@ -222,6 +226,18 @@ int dsalt_select_block_range(const float* xnorm, const float* vnorm, const int32
   if (seq_len > 0x7fffff00LL) return fail(DSALT_ERR_UNSUPPORTED, "select range: sequence too long");
   return launch_select_range(xnorm, vnorm, w, alpha, seq_len, n_heads, n_kv, k, block, set_lo, set_hi, lmk_out,
                              workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dsalt_select_shard_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block) {
+  return select_shard_workspace_bytes(seq_len, n_heads, n_kv, k, block);
+}
+
+int dsalt_select_shard(int phase, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                       int64_t seq_len, int n_heads, int n_kv, int k, int block, int rank, int n_ranks,
+                       void* workspace, size_t workspace_bytes, const void* const* peer_workspaces, int32_t* lmk_out,
+                       void* stream) {
+  return launch_select_shard(phase, xnorm, vnorm, w, alpha, seq_len, n_heads, n_kv, k, block, rank, n_ranks, workspace,
+                             workspace_bytes, peer_workspaces, lmk_out, reinterpret_cast<cudaStream_t>(stream));
 }
 
 // plan | gathered landmark K tiles | V tiles

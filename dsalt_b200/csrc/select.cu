@@ -131,12 +131,12 @@ __device__ __forceinline__ DD block_dd_sum(DD v, DD* red) {
 __global__ void __launch_bounds__(256) chunk_sums_kernel(const float* __restrict__ xn, const float* __restrict__ vn,
                                                          int n_kv, const int32_t* __restrict__ cu, int n_seqs,
                                                          const int32_t* __restrict__ base, int C, int n_chunks,
-                                                         Partial* __restrict__ part) {
+                                                         Partial* __restrict__ part, int c_lo = 0) {
   const int nsig = 1 + n_kv;
   const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (wid >= (int64_t)n_chunks * nsig) return;
-  const int c = (int)(wid / nsig), sig = (int)(wid % nsig);
+  const int c = c_lo + (int)(wid / nsig), sig = (int)(wid % nsig);
   const int total = base[n_seqs];
   Partial out{0.0, 0.0, 0.0, 0.0};
   if (c < total) {
@@ -562,15 +562,15 @@ __global__ void __launch_bounds__(256) dominance_hist_kernel(
 __global__ void __launch_bounds__(512) dominance_hist_all_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w, int n_kv,
     const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
-    const float* __restrict__ edges, int32_t* __restrict__ G, int gpb) {
+    const float* __restrict__ edges, int32_t* __restrict__ G, int gpb, int c_lo = 0) {
   // grids with rows padded to NBIN+1 entries, so that column scans hit distinct banks
   constexpr int RS = NBIN + 1;
   extern __shared__ int32_t hs[];
-  // this CTA: kv groups [g0, g0 + gpb) of chunk blockIdx.x
+  // this CTA: kv groups [g0, g0 + gpb) of chunk c_lo + blockIdx.x
   int32_t* hist = hs;                                            // [gpb][NBIN][RS]
   float* ev = reinterpret_cast<float*>(hs + gpb * NBIN * RS);    // [gpb][NBIN-1]
   __shared__ float ex[NBIN - 1];
-  const int c = blockIdx.x, nsig = 1 + n_kv, g0 = blockIdx.y * gpb;
+  const int c = c_lo + blockIdx.x, nsig = 1 + n_kv, g0 = blockIdx.y * gpb;
   const int total = base[n_seqs];
   if (c >= total) return;
   const int s = find_seq(base, n_seqs, c);
@@ -752,11 +752,11 @@ __global__ void __launch_bounds__(512) survivor_all_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w, int n_kv,
     const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base, int C,
     const float* __restrict__ edges, const int32_t* __restrict__ D, int k, int32_t* __restrict__ surv_cnt,
-    int4* __restrict__ surv_rec, int gpb) {
+    int4* __restrict__ surv_rec, int gpb, int c_lo = 0) {
   extern __shared__ float es[];  // [gpb][NBIN-1]
   __shared__ float ex[NBIN - 1];
   __shared__ int32_t cnt[32];
-  const int c = blockIdx.x, nsig = 1 + n_kv, g0 = blockIdx.y * gpb;
+  const int c = c_lo + blockIdx.x, nsig = 1 + n_kv, g0 = blockIdx.y * gpb;
   const int total = base[n_seqs];
   if (c >= total) return;
   const int s = find_seq(base, n_seqs, c);
@@ -1140,6 +1140,179 @@ int launch_select_range(const float* xnorm, const float* vnorm, const int32_t* w
   return launch_select(DSALT_SELECT_BLOCK_CAUSAL, xnorm, vnorm, w, alpha, cu, 1, Tp, (int)Tp, n_heads, n_kv, k, block,
                        lmk_out, nullptr, nullptr, reinterpret_cast<char*>(workspace) + 256, ws_bytes - 256, stream,
                        set_lo, set_hi);
+}
+
+// ---------------------------------------------------------------------------
+// Sequence-sharded block-causal selection: one sequence of seq_len positions split into
+// n_ranks contiguous shards of whole blocks, rank r owning chunks (= blocks = landmark
+// sets) [r·cpr, (r+1)·cpr). Each rank computes the per-chunk records (partial sums,
+// dominance grids, survivors) of its own chunks only and reads what it needs of the other
+// ranks' from their workspaces (same layout on every rank: a peer's region is its
+// workspace pointer plus the same offset; plain loads, peers mapped by CUDA IPC). The
+// phases are separated by the caller's cross-GPU barriers:
+//   1  chunk sums of the own chunks
+//   2  the other ranks' chunk sums; prefix statistics of every chunk and the dominance-grid
+//      thresholds from the whole sequence's statistics (identical on every rank); the
+//      dominance grids of the own chunks and their total
+//   3  the own chunks' exclusive prefix of the grids, started from the totals of the
+//      earlier ranks; survivors of the own chunks
+//   4  the survivor records of the earlier ranks' chunks; the own sets' top-k
+// Results equal dsalt_select_landmarks(DSALT_SELECT_BLOCK_CAUSAL) on the whole sequence.
+// ---------------------------------------------------------------------------
+struct ShardLayout {
+  SelectLayout L;
+  size_t cu_off, tot_off, total;
+  int n_chunks;
+};
+
+static ShardLayout shard_layout(int64_t seq_len, int n_heads, int n_kv, int k, int block) {
+  ShardLayout S{};
+  S.L = select_layout(DSALT_SELECT_BLOCK_CAUSAL, seq_len, 1, n_heads, n_kv, k, block);
+  size_t off = S.L.total;
+  S.cu_off = off;
+  off = align256(off + 2 * sizeof(int32_t));
+  S.tot_off = off;
+  off = align256(off + sizeof(int32_t) * (size_t)n_kv * NCELL);
+  S.total = off;
+  S.n_chunks = (int)((seq_len + block - 1) / block);
+  return S;
+}
+
+// the other ranks' chunk sums, from their workspaces
+__global__ void gather_partials_kernel(Partial* __restrict__ part, const char* const* __restrict__ ws_peers,
+                                       size_t part_off, int nsig, int n_chunks, int cpr, int rank) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n_chunks * nsig) return;
+  const int owner = (int)(i / nsig) / cpr;
+  if (owner == rank) return;
+  part[i] = reinterpret_cast<const Partial*>(ws_peers[owner] + part_off)[i];
+}
+
+// per (group, cell): sum of the grids of chunks [c_lo, c_hi)
+__global__ void dominance_total_kernel(const int32_t* __restrict__ G, int c_lo, int c_hi, int n_kv,
+                                       int32_t* __restrict__ tot) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_kv * NCELL) return;
+  const int g = i / NCELL, cell = i % NCELL;
+  const int64_t stride = (int64_t)n_kv * NCELL;
+  const int32_t* p = G + ((int64_t)c_lo * n_kv + g) * NCELL + cell;
+  int run = 0;
+  for (int c = c_lo; c < c_hi; c += 16) {
+    int v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = c + j < c_hi ? p[(int64_t)(c - c_lo + j) * stride] : 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) run += v[j];
+  }
+  tot[i] = run;
+}
+
+// exclusive prefix over chunks [c_lo, c_hi), started from the totals of ranks 0..rank-1
+__global__ void dominance_scan_shard_kernel(int32_t* __restrict__ G, int c_lo, int c_hi, int n_kv,
+                                            const char* const* __restrict__ ws_peers, size_t tot_off, int rank) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_kv * NCELL) return;
+  const int g = i / NCELL, cell = i % NCELL;
+  int run = 0;
+  for (int r = 0; r < rank; ++r) run += reinterpret_cast<const int32_t*>(ws_peers[r] + tot_off)[i];
+  const int64_t stride = (int64_t)n_kv * NCELL;
+  int32_t* p = G + ((int64_t)c_lo * n_kv + g) * NCELL + cell;
+  for (int c = c_lo; c < c_hi; c += 16) {
+    int v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = c + j < c_hi ? p[(int64_t)(c - c_lo + j) * stride] : 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (c + j < c_hi) p[(int64_t)(c - c_lo + j) * stride] = run;
+      run += v[j];
+    }
+  }
+}
+
+// survivor counts and records of chunks [0, c_hi) owned by other ranks, from their workspaces
+__global__ void gather_survivors_kernel(int32_t* __restrict__ cnt, int4* __restrict__ recs,
+                                        const char* const* __restrict__ ws_peers, size_t cnt_off, size_t rec_off,
+                                        int n_kv, int C, int cpr) {
+  const int c = blockIdx.x, g = blockIdx.y, owner = c / cpr;
+  const int64_t cg = (int64_t)c * n_kv + g;
+  const int n = reinterpret_cast<const int32_t*>(ws_peers[owner] + cnt_off)[cg];
+  if (threadIdx.x == 0) cnt[cg] = n;
+  const int4* src = reinterpret_cast<const int4*>(ws_peers[owner] + rec_off) + cg * C;
+  int4* dst = recs + cg * C;
+  for (int j = threadIdx.x; j < n && j < C; j += blockDim.x) dst[j] = src[j];
+}
+
+size_t select_shard_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block) {
+  if (seq_len < 1 || n_heads < 1 || n_kv < 1 || k < 0 || block <= 0) return 0;
+  return shard_layout(seq_len, n_heads, n_kv, k, block).total;
+}
+
+int launch_select_shard(int phase, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                        int64_t seq_len, int n_heads, int n_kv, int k, int block, int rank, int n_ranks, void* workspace,
+                        size_t ws_bytes, const void* const* ws_peers, int32_t* lmk_out, cudaStream_t stream) {
+  if (phase < 1 || phase > 4) return fail(DSALT_ERR_INVALID, "select shard: phase %d not in 1..4", phase);
+  if (n_ranks < 1 || rank < 0 || rank >= n_ranks || n_heads < 1 || n_kv < 1 || n_heads % n_kv || k < 0)
+    return fail(DSALT_ERR_INVALID, "select shard: bad sizes");
+  if (block < 32 || block > 1024 || block % 32) return fail(DSALT_ERR_UNSUPPORTED, "select shard: block");
+  if (seq_len < 1 || seq_len > 0x7fffff00LL || seq_len % ((int64_t)block * n_ranks))
+    return fail(DSALT_ERR_UNSUPPORTED, "select shard: seq_len must split into whole blocks per rank");
+  if (k > MAX_K) return fail(DSALT_ERR_UNSUPPORTED, "select shard: k=%d above %d", k, MAX_K);
+  if (n_kv > 32) return fail(DSALT_ERR_UNSUPPORTED, "select shard: more than 32 kv groups");
+  if (!xnorm || !vnorm || !w || !alpha || !workspace || !ws_peers || (phase == 4 && !lmk_out))
+    return fail(DSALT_ERR_INVALID, "select shard: null pointer");
+  const ShardLayout S = shard_layout(seq_len, n_heads, n_kv, k, block);
+  if (ws_bytes < S.total) return fail(DSALT_ERR_WORKSPACE, "select shard: workspace %zu < %zu", ws_bytes, S.total);
+  if (k == 0) {
+    if (phase == 4) return fail(DSALT_ERR_UNSUPPORTED, "select shard: k = 0");
+    return DSALT_OK;
+  }
+  int rc = select_set_up_attributes();
+  if (rc) return rc;
+  if ((rc = upload_bin_table())) return rc;
+  const SelectLayout& L = S.L;
+  char* ws = reinterpret_cast<char*>(workspace);
+  int32_t* cbase = reinterpret_cast<int32_t*>(ws + L.base_off);
+  int32_t* cu = reinterpret_cast<int32_t*>(ws + S.cu_off);
+  Partial* part = reinterpret_cast<Partial*>(ws + L.part_off);
+  double2* stats = reinterpret_cast<double2*>(ws + L.stats_off);
+  float* edges = reinterpret_cast<float*>(ws + L.edges_off);
+  int32_t* G = reinterpret_cast<int32_t*>(ws + L.G_off);
+  int32_t* cnt = reinterpret_cast<int32_t*>(ws + L.cnt_off);
+  int4* recs = reinterpret_cast<int4*>(ws + L.pos_off);
+  int32_t* tot = reinterpret_cast<int32_t*>(ws + S.tot_off);
+  const char* const* peers = reinterpret_cast<const char* const*>(ws_peers);
+  const int C = block, nsig = 1 + n_kv;
+  const int cpr = S.n_chunks / n_ranks, c_lo = rank * cpr, c_hi = c_lo + cpr;
+  const int gpb = n_kv % 4 == 0 ? 4 : (n_kv % 2 == 0 ? 2 : 1);
+  if (phase == 1) {
+    prefix_cu_kernel<<<1, 32, 0, stream>>>(cu, (int)seq_len);
+    chunk_table_kernel<<<1, 1024, 0, stream>>>(cu, 1, C, cbase);
+    chunk_sums_kernel<<<(unsigned)(((int64_t)cpr * nsig + 7) / 8), 256, 0, stream>>>(xnorm, vnorm, n_kv, cu, 1, cbase,
+                                                                                   C, cpr, part, c_lo);
+  } else if (phase == 2) {
+    const int64_t np = (int64_t)S.n_chunks * nsig;
+    if (n_ranks > 1)
+      gather_partials_kernel<<<(unsigned)((np + 255) / 256), 256, 0, stream>>>(part, peers, L.part_off, nsig,
+                                                                              S.n_chunks, cpr, rank);
+    block_stats_kernel<<<dim3(1, nsig), 256, 0, stream>>>(part, cu, 1, cbase, nsig, C, stats, edges);
+    const size_t smh = (size_t)gpb * (NBIN * (NBIN + 1) * sizeof(int32_t) + (NBIN - 1) * sizeof(float));
+    dominance_hist_all_kernel<<<dim3(cpr, n_kv / gpb), 512, smh, stream>>>(xnorm, vnorm, w, n_kv, cu, 1, cbase, C,
+                                                                           edges, G, gpb, c_lo);
+    dominance_total_kernel<<<(unsigned)((n_kv * NCELL + 255) / 256), 256, 0, stream>>>(G, c_lo, c_hi, n_kv, tot);
+  } else if (phase == 3) {
+    dominance_scan_shard_kernel<<<(unsigned)((n_kv * NCELL + 255) / 256), 256, 0, stream>>>(G, c_lo, c_hi, n_kv,
+                                                                                            peers, S.tot_off, rank);
+    survivor_all_kernel<<<dim3(cpr, n_kv / gpb), 512, (size_t)gpb * (NBIN - 1) * sizeof(float), stream>>>(
+        xnorm, vnorm, w, n_kv, cu, 1, cbase, C, edges, G, k, cnt, recs, gpb, c_lo);
+  } else {
+    if (c_lo > 0)
+      gather_survivors_kernel<<<dim3(c_lo, n_kv), 64, 0, stream>>>(cnt, recs, peers, L.cnt_off, L.pos_off, n_kv, C,
+                                                                   cpr);
+    const size_t sm3 = sizeof(uint64_t) * BSEL_KEY_CAP;
+    block_select_kernel<<<dim3(cpr, n_heads), BSEL_THREADS, sm3, stream>>>(
+        xnorm, vnorm, w, alpha, cu, 1, cbase, C, n_heads, n_kv, k, stats, G, cnt, recs, lmk_out, c_lo, cpr);
+  }
+  return check_cuda(cudaGetLastError(), "select shard launch");
 }
 
 int select_set_up_attributes() {

@@ -317,6 +317,31 @@ def select_block_range(xnorm, vnorm, w, alpha, k_lmk: int, n_heads: int, block: 
     return out
 
 
+def select_shard_workspace_bytes(seq_len: int, n_heads: int, n_kv: int, k_lmk: int, block: int) -> int:
+    return L.query("dsalt_select_shard_workspace_bytes", seq_len, n_heads, n_kv, k_lmk, block)
+
+
+def select_shard(phase: int, xnorm, vnorm, w, alpha, k_lmk: int, n_heads: int, block: int, rank: int, n_ranks: int,
+                 workspace, peer_workspaces, lmk_out=None):
+    """One phase (1-4) of the rank-distributed block-causal selection (``dsalt_select_shard``).
+
+    ``xnorm [L]``, ``vnorm [L, n_kv]``, ``w [L]`` are whole-sequence arrays holding (at least)
+    this rank's shard; ``workspace`` is this rank's, ``peer_workspaces`` an int64 device
+    tensor of every rank's workspace pointer. Phases run in order with a cross-GPU barrier
+    between them; phase 4 writes ``lmk_out [n_heads, blocks per rank, k_lmk]`` (allocated
+    when not given) and returns it."""
+    _cuda(xnorm, vnorm, w, alpha, workspace, peer_workspaces)
+    Lseq = int(xnorm.shape[0])
+    n_kv = int(vnorm.shape[1])
+    if phase == 4 and lmk_out is None:
+        cpr = Lseq // block // n_ranks
+        lmk_out = torch.empty(n_heads, cpr, k_lmk, dtype=torch.int32, device=xnorm.device)
+    L.call("dsalt_select_shard", int(phase), _ptr(xnorm), _ptr(vnorm), _ptr(w), _ptr(alpha), Lseq, n_heads, n_kv,
+           int(k_lmk), int(block), int(rank), int(n_ranks), _ptr(workspace), workspace.numel(), _ptr(peer_workspaces),
+           _ptr(lmk_out), _stream())
+    return lmk_out
+
+
 def attention_sharded(q, k, v, q_pos0: int, kv_pos0: int, seq_len: int, w, lmk, lmk_block: int, lmk_k_src,
                       lmk_v_src, rows_per_src: int, *, lmk_bias=None, out=None, workspace=None):
     """One rank's share of a sequence-sharded attention (``dsalt_attention_fwd_sharded``).

@@ -9,9 +9,12 @@ projections outside this module. Per step:
 2. a device-side barrier across the GPUs, then every rank pulls the other ranks' compact
    signals (``w``, ``‖x‖``, value norms: 4·(2+H_kv) bytes per token) over NVLink, so every
    rank holds them for the whole sequence (or one grouped NCCL all-gather);
-3. the block-causal landmark sets of the rank's own 512-query blocks
-   (``dsalt_select_block_range``: block ``b`` uses the prefix ``[0, b·512)``, as
-   ``results/causal_landmark_check.py:176-186``);
+3. the block-causal landmark sets of the rank's own 512-query blocks (block ``b`` uses the
+   prefix ``[0, b·512)``, as ``results/causal_landmark_check.py:176-186``). With the peer
+   exchange the selection's per-block work is spread over the ranks
+   (``dsalt_select_shard``): each rank sums, bins and prunes only its own blocks and reads
+   the other ranks' block records from their memory between device-side barriers; with
+   NCCL each rank runs ``dsalt_select_block_range`` over its whole prefix;
 4. the window halo: the previous rank's last ``n_max - 1`` K/V rows, copied into the rows
    in front of the local shard;
 5. the attention of the local queries (``dsalt_attention_fwd_sharded``): window tiles from
@@ -168,6 +171,11 @@ class ShardedCore:
         self._epoch = 0
         L_ = ops.L
         nsel = L_.query("dsalt_select_block_range_workspace_bytes", seq_len, n_heads, n_kv, k_lmk, block, p.set_hi)
+        nshard = ops.select_shard_workspace_bytes(seq_len, n_heads, n_kv, k_lmk, block)
+        # the distributed selection's workspace: the same size on every rank, read by peers
+        self._ws_shard = torch.empty(max(nshard, 1), dtype=torch.uint8, device=dev)
+        self._lmk = torch.empty(n_heads, p.set_hi - p.set_lo, k_lmk, dtype=torch.int32, device=dev)
+        self._alpha_key, self._alpha_unit = None, False
         natt = L_.query("dsalt_attention_sharded_workspace_bytes", T, n_heads, k_lmk, block, head_dim)
         self._ws_sel = torch.empty(max(nsel, 1), dtype=torch.uint8, device=dev)
         self._ws_att = torch.empty(max(natt, 1), dtype=torch.uint8, device=dev)
@@ -180,7 +188,7 @@ class ShardedCore:
         """Peer pointer tables (CUDA IPC; own entries local): K / V shards, the signal
         arrays' slices, the barrier flags."""
         T, r = self.plan.t_local, self.rank
-        bufs = [self.k_local, self.v_local, self._sig[0], self._sig[1], self._sig[2], self._flag]
+        bufs = [self.k_local, self.v_local, self._sig[0], self._sig[1], self._sig[2], self._flag, self._ws_shard]
         mine = [self.ops.ipc_export(b) for b in bufs]
         allh = [None] * self.world
         dist.all_gather_object(allh, mine, group=self.group)
@@ -203,6 +211,7 @@ class ShardedCore:
         self._v_src = torch.tensor([a + j * T * self.n_kv * 4 for j, a in enumerate(tables[4])], dtype=torch.int64,
                                    device=dev)
         self._flags = torch.tensor(tables[5], dtype=torch.int64, device=dev)
+        self._ws_peers = torch.tensor(tables[6], dtype=torch.int64, device=dev)
 
     def close(self):
         for ptr, off in self._peers:
@@ -214,6 +223,14 @@ class ShardedCore:
         L_, ops = self.ops.L, self.ops
         L_.call("dsalt_peer_barrier", ops._ptr(self._flag), ops._ptr(self._flags), self.world, self.rank,
                 self._epoch, ops._stream())
+
+    def _alpha_in_unit(self, alpha) -> bool:
+        """Whether every head's alpha lies in [0, 1] (read once per alpha tensor version)."""
+        key = (alpha.data_ptr(), alpha._version)
+        if key != self._alpha_key:
+            self._alpha_unit = bool(((alpha >= 0) & (alpha <= 1)).all())
+            self._alpha_key = key
+        return self._alpha_unit
 
     def _raise_if_failed(self):
         st = int(self._status_host[0])
@@ -248,22 +265,36 @@ class ShardedCore:
         w, xn, vn = self._sig
         row_bytes = self.k_local.stride(0) * self.k_local.element_size()
         if self.exchange == "peer":
-            # 2. every rank's signals and K / V are written
+            H, k, B, P, r = self.n_heads, self.k_lmk, self.block, self.world, self.rank
+            sel = (xn, vn, w, alpha, k, H, B, r, P, self._ws_shard, self._ws_peers)
+            # chunk sums of the own blocks
+            ops.select_shard(1, *sel)
+            # 2. every rank's signals, sums and K / V are written
             self._barrier()
-            # 3. the other ranks' signal slices and the window halo, over NVLink
-            for dst, src, n in ((w, self._w_src, T * 4), (xn, self._x_src, T * 4), (vn, self._v_src, T * self.n_kv * 4)):
-                L.call("dsalt_peer_allgather", ops._ptr(dst), ops._ptr(src), self.world, self.rank, n, ops._stream())
+            # 3. the window halo over NVLink; the other ranks' signals only when some head is
+            #    scored without pruning (alpha outside [0, 1] reads the whole prefix)
+            if not self._alpha_in_unit(alpha):
+                for dst, src, n in ((w, self._w_src, T * 4), (xn, self._x_src, T * 4),
+                                    (vn, self._v_src, T * self.n_kv * 4)):
+                    L.call("dsalt_peer_allgather", ops._ptr(dst), ops._ptr(src), self.world, self.rank, n,
+                           ops._stream())
             if p.halo > 0:
                 src_k = self._kp[self.rank - 1] + (T - p.halo) * row_bytes
                 src_v = self._vp[self.rank - 1] + (T - p.halo) * row_bytes
                 L.call("dsalt_peer_copy", ops._ptr(self.k_ext), src_k, p.halo * row_bytes, ops._stream())
                 L.call("dsalt_peer_copy", ops._ptr(self.v_ext), src_v, p.halo * row_bytes, ops._stream())
+            # 4. selection of the own blocks, its phases between barriers
+            ops.select_shard(2, *sel)
+            self._barrier()
+            ops.select_shard(3, *sel)
+            self._barrier()
+            lmk = ops.select_shard(4, *sel, lmk_out=self._lmk)
         else:
             gather_signals(self._w, self._xn, self._vn, self.group, out=self._sig)
             exchange_halo(self.k_ext, self.v_ext, p, self.halo_next, self.group)
-        # 4. landmark sets of the own blocks
-        lmk = ops.select_block_range(xn, vn, w, alpha, self.k_lmk, self.n_heads, self.block, p.set_lo, p.set_hi,
-                                     workspace=self._ws_sel)
+            # 4. landmark sets of the own blocks
+            lmk = ops.select_block_range(xn, vn, w, alpha, self.k_lmk, self.n_heads, self.block, p.set_lo, p.set_hi,
+                                         workspace=self._ws_sel)
         # 5. attention of the own queries (landmark rows read from their owners)
         ops.attention_sharded(q, self.k_ext, self.v_ext, p.q_pos0, p.kv_pos0, p.seq_len, w, lmk, self.block,
                               self.k_src, self.v_src, p.t_local, out=self.out, workspace=self._ws_att)

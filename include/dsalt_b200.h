@@ -138,7 +138,8 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
  *   dsalt_select_landmarks(DSALT_SELECT_BLOCK_CAUSAL) for those blocks. lmk_out
  *   [n_heads, set_hi - set_lo, k].
  * dsalt_attention_fwd_sharded: queries = positions [q_pos0, q_pos0 + q_rows) (q, out,
- *   lse rows 0..q_rows-1); k/v rows = positions [kv_pos0, kv_pos0 + kv_rows), which must
+ *   lse rows 0..q_rows-1); k/v (this GPU's memory: they are read by TMA tile loads; only
+ *   lmk_k_src / lmk_v_src may point to other GPUs) rows = positions [kv_pos0, kv_pos0 + kv_rows), which must
  *   hold every window key of the local queries (kv_pos0 <= q_pos0 - max width + 1; keys
  *   below kv_pos0 read as zero); w [seq_len] widths by position; lmk [n_heads,
  *   n_local_sets, k_lmk] positions within the sequence (one set per lmk_block local
@@ -157,6 +158,28 @@ int dsalt_select_block_range(const float* xnorm, const float* vnorm, const int32
                              int64_t seq_len, int n_heads, int n_kv, int k, int block, int set_lo, int set_hi,
                              int32_t* lmk_out, void* workspace, size_t workspace_bytes, void* stream);
 size_t dsalt_attention_sharded_workspace_bytes(int64_t q_rows, int n_heads, int k_lmk, int lmk_block, int head_dim);
+/* dsalt_select_shard: the block-causal sets of rank `rank`'s blocks, with the selection's
+ *   per-chunk work spread over the ranks (no counterpart in the reference; same sets as
+ *   dsalt_select_landmarks(DSALT_SELECT_BLOCK_CAUSAL) on the whole sequence, i.e. as
+ *   results/causal_landmark_check.py:82-113 per block). The sequence of seq_len positions
+ *   splits into n_ranks contiguous shards of seq_len / n_ranks positions, a whole number
+ *   of blocks each; rank r owns blocks (= chunks = sets) [r * cpr, (r + 1) * cpr).
+ *   xnorm [seq_len], vnorm [seq_len, n_kv], w [seq_len]: whole-sequence arrays of which
+ *   phases 1-3 read only the own shard; phase 4 reads earlier positions as well when some
+ *   alpha lies outside [0, 1] (no dominance pruning then), so gather the signals first in
+ *   that case. workspace (dsalt_select_shard_workspace_bytes, the same size on every
+ *   rank); peer_workspaces: device array of the n_ranks ranks' workspace pointers (own
+ *   entry included; peers mapped by dsalt_ipc_open). Call phases 1, 2, 3, 4 in order with
+ *   a cross-GPU barrier (dsalt_peer_barrier) between consecutive phases: 1 chunk sums of
+ *   the own blocks; 2 reads the others' sums, prefix statistics, dominance grids of the
+ *   own blocks; 3 reads the earlier ranks' grid totals, survivors of the own blocks; 4
+ *   reads the earlier ranks' survivors and writes lmk_out [n_heads, cpr, k]. A rank's
+ *   workspace must not be reused before every rank has finished phase 4. n_kv <= 32. */
+size_t dsalt_select_shard_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block);
+int dsalt_select_shard(int phase, const float* xnorm, const float* vnorm, const int32_t* w, const float* alpha,
+                       int64_t seq_len, int n_heads, int n_kv, int k, int block, int rank, int n_ranks,
+                       void* workspace, size_t workspace_bytes, const void* const* peer_workspaces, int32_t* lmk_out,
+                       void* stream);
 int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int dtype, int64_t q_rows, int n_heads,
                                 int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, int64_t q_pos0,
                                 int64_t kv_pos0, int64_t kv_rows, int64_t seq_len, const int32_t* w,

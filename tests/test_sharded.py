@@ -140,6 +140,38 @@ def test_sharded_kernels_equal_whole_sequence_on_emulated_shards():
     assert torch.equal(torch.cat(outs), full_out)
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("P,alphas", [(2, (0.2, 0.5, 0.6, 0.9)), (4, (0.6, 0.0, 1.0, -0.5))])
+def test_select_shard_phases_equal_whole_sequence_on_emulated_ranks(P, alphas):
+    """The rank-distributed block-causal selection (dsalt_select_shard) with P ranks emulated
+    on one GPU: every rank's workspace is a separate buffer, the peer table points at all of
+    them, and the phases run phase by phase over the ranks (what the cross-GPU barriers
+    order on P GPUs). The sets equal the whole-sequence selection bit for bit; alpha outside
+    [0, 1] takes the unpruned path (every prefix position scored)."""
+    from dsalt_b200 import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(17 + P)
+    L, H, n_kv, k, B = 16384, 4, 2, 64, 512
+    w = torch.randint(1, 400, (L,), device=dev, generator=g, dtype=torch.int32)
+    xn = 30 + torch.randn(L, device=dev, generator=g)
+    vn = 1 + 0.1 * torch.randn(L, n_kv, device=dev, generator=g)
+    alpha = torch.tensor(alphas, device=dev)
+    cu = torch.tensor([0, L], dtype=torch.int32, device=dev)
+    full = ops.select_landmarks(xn, vn, w, alpha, cu, k, H, mode="block_causal", block=B, cu_list=[0, L])
+    nbytes = ops.select_shard_workspace_bytes(L, H, n_kv, k, B)
+    ws = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(P)]
+    peers = torch.tensor([t.data_ptr() for t in ws], dtype=torch.int64, device=dev)
+    sets = [None] * P
+    for phase in (1, 2, 3, 4):
+        for r in range(P):
+            out = ops.select_shard(phase, xn, vn, w, alpha, k, H, B, r, P, ws[r], peers)
+            if phase == 4:
+                sets[r] = out
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert torch.equal(torch.cat(sets, dim=1), full)
+
+
 def _gpu_rank_main(rank, world, port, out_q, exchange):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
