@@ -204,6 +204,69 @@ def cpu_baseline(x, gw, gb, alpha, q, k, v, min_s=10.0):
                       f"path), {spent:.1f} s"}
 
 
+def masked_sdpa_baselines(budget_s=60.0):
+    """The reference's masked-SDPA CPU path (``oracle/cpu_baseline.py::masked_sdpa_step``:
+    widths, hybrid scores, the ``[T, T]`` window ∪ landmark mask, masked SDPA) on all host
+    cores, fp32, at configs[0] (cfg1), configs[1] (cfg2: 4 × 8192 packed) and the cfg4
+    recipe (H 16, d_model 1024, n_max 512, k 128, one sequence; whole-sequence landmarks —
+    the fallback has no block-causal mode) at the largest L in 8192, 16384, 32768, 65536
+    that fits the time budget and half the free host memory ([T, T] masks: ~8 bytes per
+    entry). Synthetic seeded inputs of each config's shapes (q, k, v from random-init
+    projections, RoPE left out: it changes values, not cost). Median of 3 after one
+    warm-up for cfg1; one run for the larger ones. Projections are not timed."""
+    from oracle.cpu_baseline import masked_sdpa_step
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    try:
+        import psutil
+        free = psutil.virtual_memory().available
+    except Exception:
+        free = 64 << 30
+
+    def case(T, n_seq, H, dm, n_max, k, seed):
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(T, dm, generator=g)
+
+        def W(*sh):
+            return torch.randn(*sh, generator=g) * 0.02
+
+        q = (x @ W(H * 64, dm).T).view(T, H, 64)
+        kk = (x @ W(H * 64, dm).T).view(T, H, 64)
+        xwv = x @ W(H * 64, dm).T
+        alpha = torch.sigmoid(torch.full((H,), 0.4054651081081644))
+        cu = [i * (T // n_seq) for i in range(n_seq + 1)]
+        return (x, W(dm), torch.zeros(1), 16, n_max, xwv, alpha, q, kk, xwv.view(T, H, 64), k, cu)
+
+    def timed(args, reps):
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            masked_sdpa_step(*args)
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    out = {"cores": cores, "dtype": "f32", "unit": "tokens/s"}
+    t_start = time.perf_counter()
+    a1 = case(1024, 1, 4, 256, 128, 32, 1)
+    timed(a1, 1)
+    s1 = timed(a1, 3)
+    out["cfg1"] = {"T": 1024, "seconds": s1, "value": 1024 / s1}
+    a2 = case(32768, 4, 12, 768, 256, 64, 2)
+    s2 = timed(a2, 1)
+    out["cfg2"] = {"T": 32768, "seconds": s2, "value": 32768 / s2}
+    del a2
+    last = None
+    for L in (8192, 16384, 32768, 65536):
+        left = budget_s - (time.perf_counter() - t_start)
+        if 8 * L * L > free // 2 or (last is not None and last[1] * (L / last[0]) ** 2 > left):
+            break
+        sL = timed(case(L, 1, 16, 1024, 512, 128, 3), 1)
+        last = (L, sL)
+        out["cfg4_recipe_L%d" % L] = {"seconds": sL, "value": L / sL}
+    out["largest_L_cfg4_recipe"] = last[0] if last else None
+    return out
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU path (restated, see oracle/cpu_baseline.py) on
     this host's cores. A step streams the next run of consecutive 512-query blocks of the
@@ -263,8 +326,12 @@ def run_sharded(args, rank, world, local, dev):
     del x, q
     torch.cuda.synchronize()
 
+    # the step is ~25 launches: captured once into a CUDA graph (a Python host issues them
+    # more slowly than the GPUs run them at small shards)
+    core.capture(xs, gw, gb, alpha, qs)
+
     def step():
-        core.forward(xs, gw, gb, alpha, qs)
+        core.replay()
 
     for _ in range(args.warmup):
         step()
@@ -282,6 +349,15 @@ def run_sharded(args, rank, world, local, dev):
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     status = ops.device_status()
+    # per-phase breakdown of one more (uncaptured) step: CUDA events on this rank's stream,
+    # max over ranks; the GPU first sleeps ~5 ms so that every launch is queued before it runs
+    evs = []
+    torch.cuda._sleep(10_000_000)
+    core.forward(xs, gw, gb, alpha, qs, events=evs)
+    torch.cuda.synchronize()
+    breakdown = {}
+    for (_, a), (name, b) in zip(evs[:-1], evs[1:]):
+        breakdown[name] = max_over_ranks(a.elapsed_time(b), world)
 
     # dominant kernel: this rank's attention alone
     w, xn, vn = None, None, None
@@ -314,7 +390,7 @@ def run_sharded(args, rank, world, local, dev):
         qs.copy_(qh, non_blocking=True)
         core.k_local.copy_(kh, non_blocking=True)
         core.v_local.copy_(vh, non_blocking=True)
-        o, _ = core.forward(xs, gw, gb, alpha, qs)
+        o, _ = core.replay()
         oh.copy_(o, non_blocking=True)
 
     for _ in range(2):
@@ -345,7 +421,9 @@ def run_sharded(args, rank, world, local, dev):
                 "roofline": {"bound": "hbm", "kernel": "attn_fwd_tc_kernel (one rank's shard)", "achieved": achieved,
                              "peak": hbm, "peak_source": src, "unit": "GB/s", "frac": achieved / hbm,
                              "traffic": None, "algorithmic_bytes": att_bytes, "kernel_ms": att_ms},
-                "gpu_launches": 13 * args.steps}
+                "step_breakdown_ms": {"max over ranks, one step": breakdown},
+                # rank 0 per step: signals 1, selection 10 (4 phases), barriers 4, attention 3
+                "gpu_launches": 18 * args.steps}
         print(json.dumps(line), flush=True)
     core.close()
     torch.distributed.barrier()
@@ -492,6 +570,7 @@ def main():
                 "gpu_launches": 13 * args.steps}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(x, gw, gb, alpha, q, kk, v)
+            line["cpu_baseline"]["masked_sdpa"] = masked_sdpa_baselines()
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

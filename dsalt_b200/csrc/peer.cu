@@ -11,15 +11,25 @@ namespace dsalt {
 
 // rank `rank` publishes `epoch` in its own flag, then waits until every rank's flag has
 // reached it. Writes made by this GPU before the call are visible to the peers after it.
-__global__ void peer_barrier_kernel(int* own_flag, const int* const* flags, int n_ranks, int rank, int epoch,
+// epoch <= 0: the epoch is own_flag[1] + 1, stored back in own_flag[1] (a device-side
+// counter, so that a captured CUDA graph advances it on every replay).
+__global__ void peer_barrier_kernel(int* own_flag, const int* const* flags, int n_ranks, int rank, int epoch_arg,
                                     int* err) {
+  __shared__ int s_epoch;
   const int t = threadIdx.x;
   if (t == 0) {
+    int epoch = epoch_arg;
+    if (epoch <= 0) {
+      epoch = own_flag[1] + 1;
+      own_flag[1] = epoch;
+    }
+    s_epoch = epoch;
     __threadfence_system();
     *reinterpret_cast<volatile int*>(own_flag) = epoch;
     __threadfence_system();
   }
   __syncthreads();
+  const int epoch = s_epoch;
   if (t < n_ranks && t != rank) {
     const volatile int* f = reinterpret_cast<const volatile int*>(flags[t]);
     const uint64_t t0 = globaltimer_ns();

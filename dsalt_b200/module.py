@@ -23,6 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import library  # noqa: F401  (registers torch.ops.dsalt_b200.*)
 from . import ops
 
 
@@ -87,7 +88,9 @@ class DSALTAttention(nn.Module):
     def forward(self, x, cu_seqlens=None, max_seqlen=None, rope_cs=None, cu_list=None):
         """Packed inference forward ``-> (out [T, d_model], aux 0)``. ``max_seqlen`` is
         accepted for signature compatibility and not needed: the kernels derive every
-        sequence length from ``cu_seqlens`` (or ``cu_list``)."""
+        sequence length from ``cu_seqlens`` (or ``cu_list``). Under ``torch.compile`` pass
+        ``cu_list`` (the host list of ``cu_seqlens``): reading it from the device tensor is a
+        host synchronisation, which a compiled graph cannot contain."""
         if cu_seqlens is None:
             raise NotImplementedError("dsalt_b200 implements the packed path; pass cu_seqlens")
         if self.training:
@@ -120,12 +123,14 @@ class DSALTAttention(nn.Module):
         # value norms use x·W_Vᵀ, which is the v_proj output when there is no bias
         vs = v if self.v_proj.bias is None else F.linear(x, self.v_proj.weight.to(v.dtype))
         norm_round = (x.dtype != torch.float32) and not amp
-        w, xn, vn = ops.window_signals(x, gw, gb, self.n_min, self.n_max, vs, D, norm_round, logit=logit)
+        # the operators as registered torch.library ops: opaque nodes under torch.compile
+        w, xn, vn = torch.ops.dsalt_b200.window_signals(x, gw, gb, self.n_min, self.n_max, vs, D, norm_round, logit)
         alpha = self._alpha().detach().float()
         mode = "global" if self.selection == "global" else "block_causal"
-        lmk = ops.select_landmarks(xn, vn, w, alpha, cu_seqlens, self.k_lmk, H, mode, self.block, cu_list=cu_h)
-        out = ops.dsalt_attention(q.contiguous(), k.contiguous(), v.contiguous(), lmk, None, w, cu_seqlens,
-                                  lmk_block=0 if mode == "global" else self.block, out_dtype=q.dtype, cu_list=cu_h)
+        lmk = torch.ops.dsalt_b200.select_landmarks(xn, vn, w, alpha, cu_seqlens, self.k_lmk, H, mode, self.block,
+                                                    cu_h)
+        out = torch.ops.dsalt_b200.dsalt_attention(q.contiguous(), k.contiguous(), v.contiguous(), lmk, None, w,
+                                                   cu_seqlens, 0 if mode == "global" else self.block, cu_h, q.dtype)
         self._last_P = None
         aux = torch.zeros((), device=x.device, dtype=x.dtype)
         return self.out_proj(out.view(T, self.d_model).to(self.out_proj.weight.dtype)), aux

@@ -183,6 +183,7 @@ class ShardedCore:
         self._open_peers()
         self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._status_event = None
+        self._graph, self._graph_res = None, None
 
     def _open_peers(self):
         """Peer pointer tables (CUDA IPC; own entries local): K / V shards, the signal
@@ -214,15 +215,16 @@ class ShardedCore:
         self._ws_peers = torch.tensor(tables[6], dtype=torch.int64, device=dev)
 
     def close(self):
+        self._graph = None  # the graph's kernels hold peer pointers: release it first
         for ptr, off in self._peers:
             self.ops.ipc_close(ptr, off)
         self._peers = []
 
     def _barrier(self):
-        self._epoch += 1
+        # the epoch comes from the device counter in _flag[1] (graph replays advance it)
         L_, ops = self.ops.L, self.ops
-        L_.call("dsalt_peer_barrier", ops._ptr(self._flag), ops._ptr(self._flags), self.world, self.rank,
-                self._epoch, ops._stream())
+        L_.call("dsalt_peer_barrier", ops._ptr(self._flag), ops._ptr(self._flags), self.world, self.rank, 0,
+                ops._stream())
 
     def _alpha_in_unit(self, alpha) -> bool:
         """Whether every head's alpha lies in [0, 1] (read once per alpha tensor version)."""
@@ -247,21 +249,71 @@ class ShardedCore:
             self._status_event.synchronize()
             self._raise_if_failed()
 
-    def forward(self, x, gate_weight, gate_bias, alpha, q, check: bool = False):
+    def forward(self, x, gate_weight, gate_bias, alpha, q, check: bool = False, events=None):
         """``x [T_local, d_model]`` and ``q [T_local, H, D]`` of this rank's positions (``k_local`` /
         ``v_local`` already written). Returns this rank's attention output ``[T_local, H, D]``
         and its landmark sets. Raises when an earlier step's status read has completed with a
-        non-zero status; ``check=True`` also waits for this step and checks it."""
+        non-zero status; ``check=True`` also waits for this step and checks it. ``events``
+        (a list) receives ``(phase name, CUDA event)`` pairs recorded after each phase, for a
+        per-phase time breakdown."""
+        if self._status_event is not None and self._status_event.query():
+            self._raise_if_failed()
+        out, lmk = self._step(x, gate_weight, gate_bias, alpha, q, events)
+        self._read_status()
+        if check:
+            self.check()
+        return out, lmk
+
+    def _read_status(self):
+        # the device status word, read without stalling the stream
+        self.ops.L.call("dsalt_device_status_async", self._status_host.data_ptr(), self.ops._stream())
+        if self._status_event is None:
+            self._status_event = torch.cuda.Event()
+        self._status_event.record()
+
+    def capture(self, x, gate_weight, gate_bias, alpha, q):
+        """Record one step into a CUDA graph (peer exchange only): the step is ~25 launches,
+        which a Python host issues more slowly than the GPUs run them once the shards are
+        small. The graph keeps the pointers of ``x``, ``q``, ``k_local`` / ``v_local`` and of
+        the weights: write new inputs into those tensors and call :meth:`replay`. Every rank
+        captures together (the capture runs one ordinary step first, with its barriers)."""
+        if self.exchange != "peer":
+            raise ValueError("graph capture needs exchange='peer'")
+        self.forward(x, gate_weight, gate_bias, alpha, q)  # first-call set-up outside the capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        # library set-up calls made outside the stream (function attributes, device queries)
+        # are allowed during the capture
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            res = self._step(x, gate_weight, gate_bias, alpha, q)
+        self._graph, self._graph_res = g, res
+
+    def replay(self):
+        """One step from the captured graph; returns (out, landmark sets) like :meth:`forward`."""
+        if self._status_event is not None and self._status_event.query():
+            self._raise_if_failed()
+        self._graph.replay()
+        self._read_status()
+        return self._graph_res
+
+    def _step(self, x, gate_weight, gate_bias, alpha, q, events=None):
         ops, p = self.ops, self.plan
         L = ops.L
         T = p.t_local
-        if self._status_event is not None and self._status_event.query():
-            self._raise_if_failed()
+
+        def mark(name):
+            if events is not None:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                events.append((name, e))
+
+        mark("start")
         # 1. own signals, into this rank's slice of the sequence arrays
         L.call("dsalt_token_signals", ops._ptr(x), ops._dt(x), T, x.shape[1], x.stride(0),
                ops._ptr(gate_weight), ops._ptr(gate_bias), ops._dt(gate_weight), self.n_min, self.n_max,
                ops._ptr(self.v_local), ops._dt(self.v_local), self.v_local.stride(0), self.n_kv, self.head_dim,
                L.NORM_F32, ops._ptr(self._w), ops._ptr(self._xn), ops._ptr(self._vn), None, None, ops._stream())
+        mark("signals")
         w, xn, vn = self._sig
         row_bytes = self.k_local.stride(0) * self.k_local.element_size()
         if self.exchange == "peer":
@@ -269,8 +321,10 @@ class ShardedCore:
             sel = (xn, vn, w, alpha, k, H, B, r, P, self._ws_shard, self._ws_peers)
             # chunk sums of the own blocks
             ops.select_shard(1, *sel)
+            mark("select phase 1")
             # 2. every rank's signals, sums and K / V are written
             self._barrier()
+            mark("barrier 1")
             # 3. the window halo over NVLink; the other ranks' signals only when some head is
             #    scored without pruning (alpha outside [0, 1] reads the whole prefix)
             if not self._alpha_in_unit(alpha):
@@ -283,12 +337,18 @@ class ShardedCore:
                 src_v = self._vp[self.rank - 1] + (T - p.halo) * row_bytes
                 L.call("dsalt_peer_copy", ops._ptr(self.k_ext), src_k, p.halo * row_bytes, ops._stream())
                 L.call("dsalt_peer_copy", ops._ptr(self.v_ext), src_v, p.halo * row_bytes, ops._stream())
+            mark("halo")
             # 4. selection of the own blocks, its phases between barriers
             ops.select_shard(2, *sel)
+            mark("select phase 2")
             self._barrier()
+            mark("barrier 2")
             ops.select_shard(3, *sel)
+            mark("select phase 3")
             self._barrier()
+            mark("barrier 3")
             lmk = ops.select_shard(4, *sel, lmk_out=self._lmk)
+            mark("select phase 4")
         else:
             gather_signals(self._w, self._xn, self._vn, self.group, out=self._sig)
             exchange_halo(self.k_ext, self.v_ext, p, self.halo_next, self.group)
@@ -298,16 +358,11 @@ class ShardedCore:
         # 5. attention of the own queries (landmark rows read from their owners)
         ops.attention_sharded(q, self.k_ext, self.v_ext, p.q_pos0, p.kv_pos0, p.seq_len, w, lmk, self.block,
                               self.k_src, self.v_src, p.t_local, out=self.out, workspace=self._ws_att)
+        mark("attention")
         # 6. every rank is done reading the others' memory
         if self.exchange == "peer":
             self._barrier()
         else:
             dist.all_reduce(self._flag[:1], group=self.group)
-        # the device status word, read without stalling the stream
-        L.call("dsalt_device_status_async", self._status_host.data_ptr(), ops._stream())
-        if self._status_event is None:
-            self._status_event = torch.cuda.Event()
-        self._status_event.record()
-        if check:
-            self.check()
+        mark("closing barrier")
         return self.out, lmk

@@ -190,7 +190,9 @@ int dsalt_attention_fwd_sharded(const void* q, const void* k, const void* v, int
 /* dsalt_peer_barrier: rank `rank` of n_ranks GPUs (one process each) stores `epoch` in its
  *   own flag (an int in its memory) and waits until every rank's flag (peer_flags: device
  *   array of the ranks' flag pointers, peers mapped by dsalt_ipc_open) has reached it;
- *   epochs must increase from call to call. Memory written on this GPU before the call is
+ *   epochs must increase from call to call. epoch <= 0 takes the epoch from a device-side
+ *   counter in own_flag[1] (incremented by the call; own_flag then points to two ints), so
+ *   that a CUDA graph holding the call advances it on every replay. Memory written on this GPU before the call is
  *   visible to the peers' work queued after theirs. A wait longer than 2 s gives up and
  *   sets the device status word (no hang).
  * dsalt_peer_allgather: dst[j * bytes_per_rank ...] <- src[j][0 .. bytes_per_rank) for

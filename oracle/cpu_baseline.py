@@ -1,6 +1,10 @@
-"""Timed CPU baseline: the reference's block-causal forward restated with torch CPU ops.
+"""Timed CPU baselines: the reference's CPU paths restated with torch CPU ops.
 
 TEST/BENCH INFRASTRUCTURE ONLY (imported by ``bench.py``'s CPU-baseline legs).
+
+``masked_sdpa_step`` is the reference's non-Triton inference branch of ``_packed``
+(``dsalt/modules/dsalt_attention.py:619-625``): widths, hybrid scores, the ``[T, T]``
+window ∪ landmark mask and masked SDPA. ``BlockCausalCPU`` below is its block-causal path.
 
 Follows ``results/causal_landmark_check.py``: token signals (``_token_signals``
 ``:68-79``: ``‖x‖``, value norms) and window widths
@@ -139,3 +143,62 @@ class BlockCausalCPU:
             self.run_block(b)
         dt = time.perf_counter() - t0
         return min(self.T, b1 * self.B) - b0 * self.B, dt
+
+
+def masked_sdpa_step(x, gate_w, gate_b, n_min, n_max, xwv, alpha, q, k, v, k_lmk, cu):
+    """The reference's masked-SDPA inference path on CPU, op for op in torch:
+
+    * widths ``clamp(floor(n_min + σ(x·g + b)·(n_max − n_min)), min=1)``
+      (``_window_sizes``, ``dsalt_attention.py:270-284``);
+    * hybrid scores: ``z_x`` of ``‖x‖`` and ``z_v`` of the value norms over all packed tokens
+      (unbiased std, clamp 1e-6), ``s = α·z_v + (1 − α)·z_x``
+      (``hybrid_scores_per_head``, ``dsalt/kernels/landmark_tokens_ker.py:44-60``);
+      ``xwv`` is ``x·W_Vᵀ`` ``[T, n_kv·D]`` (the value projection without bias);
+    * the mask of ``_build_mask_packed`` (``dsalt_attention.py:96-144``): the causal window
+      of each row (``build_local_window_mask_packed``, ``window_utils.py:40-70``) plus, for
+      every row of a sequence, the union over heads of the sequence's top-k positions
+      among tokens outside their own window;
+    * ``sparse_attention_forward_packed`` (``dsalt/kernels/sparse_attn.py:29-56``): SDPA
+      with the additive ``-inf`` mask.
+
+    ``q, k, v`` are ``[T, H, D]`` (kv heads already repeated). Returns ``[T, H, D]``."""
+    T, H, D = q.shape
+    xf = x.float()
+    w = torch.floor(n_min + torch.sigmoid(xf @ gate_w.float() + gate_b.float()) * (n_max - n_min)).clamp(min=1)
+    x_norm = xf.norm(dim=-1)
+    z_x = (x_norm - x_norm.mean()) / x_norm.std().clamp(min=1e-6)
+    n_kv = xwv.shape[1] // D
+    vn = xwv.float().view(T, n_kv, D).norm(dim=-1)
+    z_v = (vn - vn.mean(0, keepdim=True)) / vn.std(0, keepdim=True).clamp(min=1e-6)
+    if n_kv != H:
+        z_v = z_v.repeat_interleave(H // n_kv, dim=1)
+    scores = alpha * z_v + (1.0 - alpha) * z_x.unsqueeze(1)
+    lens = torch.tensor([cu[i + 1] - cu[i] for i in range(len(cu) - 1)])
+    starts = torch.tensor(cu[:-1])
+    seq_ids = torch.repeat_interleave(torch.arange(len(cu) - 1), lens)
+    seq_off = torch.arange(T) - starts[seq_ids]
+    wl = w.long()
+    lo = (seq_off - wl + 1).clamp(min=0) + starts[seq_ids]
+    col = torch.arange(T)
+    mask = (seq_ids[:, None] == seq_ids[None, :]) & (col[None, :] >= lo[:, None]) & (col[None, :] <= col[:, None])
+    # the landmark columns as _build_mask_packed forms them (:119-142): scores padded per
+    # sequence, top-k along positions, the union over heads scattered into every row
+    s_masked = scores.masked_fill((seq_off < wl)[:, None], float("-inf"))
+    n_seqs, max_len = len(cu) - 1, int(lens.max())
+    score_pad = torch.full((n_seqs, max_len, H), float("-inf"))
+    score_pad[seq_ids, seq_off] = s_masked
+    vals, top = torch.topk(score_pad, min(k_lmk, max_len), dim=1, sorted=False)
+    valid = vals > float("-inf")
+    abs_lmk = (starts[:, None, None] + top).clamp(max=T - 1)
+    for b in range(n_seqs):
+        if not valid[b].any():
+            continue
+        a, e = cu[b], cu[b + 1]
+        idx = abs_lmk[b][valid[b]].reshape(-1).unique()
+        row_idx = torch.arange(a, e).unsqueeze(1).expand(-1, idx.shape[0])
+        col_idx = idx.unsqueeze(0).expand(e - a, -1)
+        mask[row_idx, col_idx] = True
+    additive = torch.zeros(T, T, dtype=q.dtype).masked_fill(~mask, float("-inf"))
+    o = torch.nn.functional.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                                         v.transpose(0, 1)[None], attn_mask=additive[None, None])
+    return o[0].transpose(0, 1)

@@ -36,3 +36,24 @@ def test_block_causal_cpu_baseline_matches_oracle():
             assert got == ref, (b, h)
     ref, _ = O.attention_forward(q.numpy(), kk.numpy(), v.numpy(), w, lo, [0, T], lmk_block=B)
     assert np.abs(out - ref).max() < 1e-4
+
+
+def test_masked_sdpa_step_matches_golden_pinned_port():
+    """The timed masked-SDPA restatement equals the oracle's port, which the golden test
+    pins to the reference's own fallback (configs[0] shapes)."""
+    import cases as C
+    from oracle.cpu_baseline import masked_sdpa_step
+    cfg = C.CASES["cfg1_fp32"]
+    params = C.make_params(cfg)
+    x = C.make_x(cfg)
+    q, k, v, vp = C.project(cfg, params, x)
+    cu = C.cu_seqlens(cfg)
+    alpha = C.alpha(params)
+    gw = params["win_gate.weight"].reshape(-1)
+    gb = params["win_gate.bias"]
+    out = masked_sdpa_step(x, gw, gb, cfg["n_min"], cfg["n_max"], vp, alpha, q, k, v, cfg["k"], cu)
+    w, _, _ = O.window_sizes(x.numpy(), gw.numpy(), float(gb[0]), cfg["n_min"], cfg["n_max"], "fp32")
+    xn, vn = O.token_signals(x.numpy(), vp.numpy(), cfg["Hkv"], cfg["D"], None)
+    scores, _, _ = O.global_scores(xn, vn, alpha.numpy(), cfg["H"])
+    ref = O.masked_sdpa_forward(q.numpy(), k.numpy(), v.numpy(), scores, w, cu, cfg["k"])
+    assert np.abs(out.numpy() - ref).max() < 1e-5

@@ -189,9 +189,20 @@ def _gpu_rank_main(rank, world, port, out_q, exchange):
         sl = slice(p.q_pos0, p.q_pos0 + p.t_local)
         core.k_local.copy_(kk[sl])
         core.v_local.copy_(v[sl])
+        xs, qs = x[sl].contiguous(), q[sl].contiguous()
         for _ in range(2):  # the second step reuses every buffer
-            out, lmk = core.forward(x[sl], gw, gb, alpha, q[sl].contiguous())
+            out, lmk = core.forward(xs, gw, gb, alpha, qs)
         torch.cuda.synchronize()
+        out, lmk = out.clone(), lmk.clone()
+        if exchange == "peer":
+            # the step captured into a CUDA graph and replayed (device-side barrier epochs
+            # advance on every replay): the same bits, step after step
+            core.capture(xs, gw, gb, alpha, qs)
+            for _ in range(3):
+                o2, l2 = core.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(o2, out) and torch.equal(l2, lmk)
+            core.check()
         from dsalt_b200 import ops
         out_q.put((rank, out.cpu(), lmk.cpu(), ops.device_status()))
     finally:
