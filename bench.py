@@ -430,6 +430,64 @@ def run_sharded(args, rank, world, local, dev):
     torch.distributed.destroy_process_group()
 
 
+PREFILL = {
+    # 24-layer decoder, d_model 1024, 16 heads (head_dim 64), MLP 4096, vocab
+    # 50257, w_max 256, k 64, whole-sequence selection; B = 1, L = 16384. The reference's
+    # block is SwiGLU (configs[2] says GELU): SwiGLU with d_ff 4096 is used.
+    "prefill_cfg3": dict(cfg=dict(vocab_size=50257, d_model=1024, n_layers=24, n_heads=16, n_min=16, n_max=256,
+                                  k_lmk=64, max_seq_len=16384, d_ff=4096, selection="global"), L=16384),
+    # Qwen2.5-3B-shaped graft: 36 layers, hidden 2048, 16 query / 2 kv heads
+    # (head_dim 128), SwiGLU 11008, RMSNorm, RoPE base 1e6, q/k/v bias, vocab 151936,
+    # w_max 512, k 128, block-causal; B = 1, L = 32768.
+    "prefill_cfg5": dict(cfg=dict(vocab_size=151936, d_model=2048, n_layers=36, n_heads=16, n_min=16, n_max=512,
+                                  k_lmk=128, max_seq_len=32768, d_ff=11008, n_kv_heads=2, qkv_bias=True,
+                                  rope_base=1e6, selection="block_causal", block=512, tie_weights=False), L=32768),
+}
+
+
+def run_prefill(args):
+    """Full-model prefill on one GPU: random-init bf16
+    weights, uniform random token ids from a seed, every layer's attention on this
+    package's kernels, projections / MLP / LM head as library GEMMs. A step is one forward
+    of the whole pack including the logits of every token (as the reference returns them)."""
+    from dsalt_b200.model import DSALTConfig, DSALTLMHeadModel
+    spec = PREFILL[args.workload]
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    cfg = DSALTConfig(**spec["cfg"])
+    with torch.device(dev):
+        model = DSALTLMHeadModel.from_config(cfg).to(dev, torch.bfloat16).eval()
+    L = spec["L"]
+    g = torch.Generator(device=dev).manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (L,), device=dev, generator=g)
+    cu = [0, L]
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+
+    def step():
+        return model(ids, cu_t, cu_list=cu)["logits"]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            out = step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    from dsalt_b200 import ops
+    line = {"metric": "DSALT LM prefill tokens/s", "value": L / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random token ids, random init)",
+            "config": {"workload": args.workload, "L": L, **spec["cfg"],
+                       "params": sum(p.numel() for p in model.parameters())},
+            "clocks": clk.summary(), "device_status": ops.device_status(),
+            "logits_finite": bool(torch.isfinite(out[-1].float()).all())}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -438,6 +496,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="core", choices=["core", *PREFILL],
+                    help="core: the DSALT attention core (the benchmark); prefill_cfg3 / prefill_cfg5: full-model "
+                         "prefill of BASELINE configs[2] / configs[4] on one GPU")
     ap.add_argument("--seq-len", type=int, default=CFG["L"],
                     help="sequence length (131072 is the benchmark; shorter ones for profiler captures)")
     args = ap.parse_args()
@@ -446,6 +507,9 @@ def main():
         CFG["workload"] = CFG["workload"].replace("L131072", f"L{args.seq_len}")
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "core":
+        args.warmup = max(args.warmup, 3)
+        return run_prefill(args)
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)

@@ -16,6 +16,7 @@ from .ops import (  # noqa: F401
     window_signals,
 )
 from .module import DSALTAttention  # noqa: F401
+from .model import DSALTConfig, DSALTLMHeadModel, DSALTTransformerBlock  # noqa: F401
 from ._lib import DsaltError  # noqa: F401
 
 __version__ = "0.1.0"

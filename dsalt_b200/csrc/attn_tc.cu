@@ -24,7 +24,8 @@
 //                     masked, exponentiated; P goes back to TMEM as 16-bit pairs; O is
 //                     rescaled in TMEM only when the running max grows by more than 2^8.
 // TMEM (512 columns): per pipeline S (128) | P (64) | O (head_dim).
-// Warps: 0/1 producer/MMA of A, 2/3 producer/MMA of B, 4-7 softmax A, 8-11 softmax B.
+// Warps: 0/1 producer/MMA of A, 2/3 producer/MMA of B, 4-7 softmax A, 8-11 softmax B
+// (head_dim 64); at head_dim 128 pipeline A alone: warps 0/1, 4-7 (2/3 idle).
 // Every mbarrier wait is bounded (common.cuh) and reports to the device status word.
 #include <cuda.h>
 
@@ -38,12 +39,19 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int NPIPE = 2;
+// pipelines per CTA: two at head_dim 64; one at head_dim 128, whose tiles (Q + 3 K + 2 V
+// stages of 32 KB) fill the shared memory and whose TMEM (S 128 | P 64 | O 128) takes 320
+// of the 512 columns
+template <int HD>
+struct Pipes {
+  static constexpr int N = HD == 64 ? 2 : 1;
+  static constexpr int THREADS = 128 + 128 * N;
+};
+constexpr int NPIPE_MAX = 2;
 constexpr int NSK = 3;          // K stages per pipeline (released when S = Q·Kᵀ completes)
 constexpr int NSV = 2;          // V stages per pipeline (released when O += P·V completes)
 constexpr int NQB = 1;          // Q buffers per pipeline
 constexpr int NIS = 2;          // item-description slots per pipeline
-constexpr int NTHREADS = 384;
 // Register split with setmaxnreg. The block launches with 168 registers per thread
 // (384 x 168 = 64512); warpgroup 0 (producers, MMA issuers) gives back to 88 and the two
 // softmax warpgroups take 208: 128 x 88 + 256 x 208 = 64512, and every scheduler (one
@@ -56,7 +64,7 @@ constexpr int NTHREADS = 384;
 #endif
 constexpr uint32_t REGS_CTRL = DSALT_REGS_CTRL, REGS_SOFTMAX = DSALT_REGS_SOFTMAX;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t PIPE_COLS = 256;                 // S 128 | P 64 | O 64
+constexpr uint32_t PIPE_COLS = 256;                 // S 128 | P 64 | O 64 (head_dim 64)
 constexpr uint32_t COL_S = 0, COL_P = 128, COL_O = 192;
 constexpr int MAX_LMK = 256;
 constexpr float OVERFLOW_SUM = 32768.0f;  // a tile's row sum above 2^15 (or NaN/inf) redoes the tile
@@ -189,12 +197,13 @@ struct Smem {
   static constexpr uint32_t V_OFF = K_OFF + NSK * TILE_BYTES;
   // item slots: description, per-row window widths, landmark positions
   static constexpr uint32_t SLOT_BYTES = 64 + BM * 4 + MAX_LMK * 4;
-  static constexpr uint32_t SLOT_OFF = NPIPE * PIPE_BYTES;  // + (pipe * NIS + slot) * SLOT_BYTES
-  static constexpr uint32_t BAR_OFF = SLOT_OFF + NPIPE * NIS * SLOT_BYTES;
+  static constexpr int NP = Pipes<HD>::N;
+  static constexpr uint32_t SLOT_OFF = NP * PIPE_BYTES;  // + (pipe * NIS + slot) * SLOT_BYTES
+  static constexpr uint32_t BAR_OFF = SLOT_OFF + NP * NIS * SLOT_BYTES;
   // per pipeline: q_full[NQB] q_empty[NQB] k_full[NSK] k_empty[NSK] v_full[NSV] v_empty[NSV]
   // s_full s_empty p_full o_full o_empty item_full[NIS] item_empty[NIS]
   static constexpr int NBAR_PIPE = 2 * NQB + 2 * NSK + 2 * NSV + 5 + 2 * NIS;
-  static constexpr uint32_t MISC_OFF = BAR_OFF + NPIPE * NBAR_PIPE * 8;
+  static constexpr uint32_t MISC_OFF = BAR_OFF + NP * NBAR_PIPE * 8;
   static constexpr uint32_t BYTES = MISC_OFF + 16;
 };
 
@@ -355,7 +364,7 @@ __device__ __forceinline__ uint32_t pack_p(bool bf, float lo, float hi) {
 }
 
 template <int HD, bool BF>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(Pipes<HD>::THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_lk,
                        const __grid_constant__ CUtensorMap tm_lv, const Params p) {
@@ -369,7 +378,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int n_items = (p.shard_tiles > 0 ? p.shard_tiles : p.tile_base[p.n_seqs]) * p.H;
 
   if (threadIdx.x == 0) {
-    for (int pp = 0; pp < NPIPE; ++pp) {
+    for (int pp = 0; pp < SM::NP; ++pp) {
       uint64_t* b = reinterpret_cast<uint64_t*>(sm + SM::BAR_OFF) + pp * SM::NBAR_PIPE;
       for (int i = 0; i < NQB; ++i) {
         mbar_init(b + i, 1);        // q_full
@@ -422,11 +431,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t pbase = sbase + pipe * SM::PIPE_BYTES;
   const uint32_t tpipe = tbase + pipe * PIPE_COLS;
   // items of this pipeline: the CTA's items alternate between the two pipelines
-  const int item0 = blockIdx.x + pipe * gridDim.x, istride = NPIPE * gridDim.x;
+  const int item0 = blockIdx.x + pipe * gridDim.x, istride = SM::NP * gridDim.x;
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CTRL));
-    if ((warp & 1) == 0) {
+    if constexpr (SM::NP == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CTRL));
+    if (pipe >= SM::NP) {
+      // control warps of a pipeline this head_dim does not have: idle
+    } else if ((warp & 1) == 0) {
       // ---------------------------------------------------------------- producer
       if (lane == 0) {
         tma_prefetch_desc(&tm_q);
@@ -463,8 +474,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int pos = __ldg(P + c);
             if (pos >= 0) {
               const int64_t off = (int64_t)(fn.kvb + pos) * p.kv_stride + (int64_t)fn.hk * HD;
-              prefetch_l2(kg + off);
-              prefetch_l2(vg + off);
+#pragma unroll
+              for (int a = 0; a < SM::NA; ++a) {  // one 128-byte line per 64 columns
+                prefetch_l2(kg + off + a * 64);
+                prefetch_l2(vg + off + a * 64);
+              }
             }
           }
         }
@@ -630,7 +644,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
+    if constexpr (SM::NP == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
     // ------------------------------------------------------------------ softmax
     const int quad = warp & 3;        // TMEM lane quadrant of this warp
     const int r = quad * 32 + lane;   // query row of the tile = TMEM lane
@@ -955,7 +969,8 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
                    int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
                    cudaStream_t stream, const ShardArgs* shard) {
   using namespace tc;
-  if (HD != 64) return fail(DSALT_ERR_UNSUPPORTED, "attention (tensor cores): head_dim %d not supported (64)", HD);
+  if (HD != 64 && HD != 128)
+    return fail(DSALT_ERR_UNSUPPORTED, "attention (tensor cores): head_dim %d not supported (64, 128)", HD);
   if (k_lmk > MAX_LMK) return fail(DSALT_ERR_UNSUPPORTED, "attention: k_lmk %d above %d", k_lmk, MAX_LMK);
   if (lmk_block % BM) return fail(DSALT_ERR_UNSUPPORTED, "attention: lmk_block must be a multiple of %d", BM);
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15 || (q_stride * 2) % 16 ||
@@ -1012,7 +1027,8 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
     const int nlt = (k_lmk + BN - 1) / BN;
     const int64_t tiles = (int64_t)p.n_sets_local * H * nlt;
     if (tiles > 0) {
-      lmk_gather_kernel<64><<<(unsigned)tiles, 256, 0, stream>>>(
+      auto gk = HD == 64 ? lmk_gather_kernel<64> : lmk_gather_kernel<128>;
+      gk<<<(unsigned)tiles, 256, 0, stream>>>(
           lmk, H, H / Hkv, p.n_sets_local, k_lmk, nlt, reinterpret_cast<const uint16_t* const*>(shard->lmk_k_src),
           reinterpret_cast<const uint16_t* const*>(shard->lmk_v_src), (int)shard->rows_per_src, kv_stride,
           reinterpret_cast<uint16_t*>(shard->lmk_tiles_k), reinterpret_cast<uint16_t*>(shard->lmk_tiles_v));
@@ -1035,15 +1051,19 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const int64_t max_items = (shard ? (int64_t)shard_tiles : T / BM + n_seqs) * (int64_t)H;
-  const int64_t want = (max_items + NPIPE - 1) / NPIPE;
+  const int np = HD == 64 ? Pipes<64>::N : Pipes<128>::N;
+  const int64_t want = (max_items + np - 1) / np;
   const int grid = (int)(want < nsm ? want : nsm);
   if (grid <= 0) return DSALT_OK;
-  const size_t smem = Smem<64>::BYTES + 1024;
-  auto kern = dtype == DSALT_BF16 ? attn_fwd_tc_kernel<64, true> : attn_fwd_tc_kernel<64, false>;
+  const size_t smem = (HD == 64 ? Smem<64>::BYTES : Smem<128>::BYTES) + 1024;
+  const int threads = HD == 64 ? Pipes<64>::THREADS : Pipes<128>::THREADS;
+  const bool bf = dtype == DSALT_BF16;
+  auto kern = HD == 64 ? (bf ? attn_fwd_tc_kernel<64, true> : attn_fwd_tc_kernel<64, false>)
+                       : (bf ? attn_fwd_tc_kernel<128, true> : attn_fwd_tc_kernel<128, false>);
   if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "attention smem attr")))
     return rc;
-  kern<<<grid, NTHREADS, smem, stream>>>(mq, mk, mv, mlk, mlv, p);
+  kern<<<grid, threads, smem, stream>>>(mq, mk, mv, mlk, mlv, p);
   return check_cuda(cudaGetLastError(), "attention launch");
 }
 

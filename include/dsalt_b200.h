@@ -111,8 +111,9 @@ int dsalt_select_landmarks(int mode, const float* xnorm, const float* vnorm, con
  *   _build_seq_block_map (selectors.py:37-67), which are done inside.
  *
  * q [T, n_heads, head_dim], k/v [T, n_kv, head_dim] (token strides q_stride, kv_stride in
- *   elements; heads contiguous), dtype DSALT_BF16 / DSALT_F16 (tensor cores) or DSALT_F32
- *   (fp32 CUDA cores). GQA: head h uses kv head h / (n_heads / n_kv).
+ *   elements; heads contiguous), dtype DSALT_BF16 / DSALT_F16 (tensor cores; head_dim 64 or
+ *   128) or DSALT_F32 (fp32 CUDA cores; head_dim 32, 64, 128 or 256). GQA: head h uses kv
+ *   head h / (n_heads / n_kv).
  * w [T] int32 window widths (clamped to >= 1 inside).
  * lmk [n_heads, n_sets, k_lmk] int32 positions within the sequence, -1 = none. For the
  *   bf16/fp16 path every set must list its positions ascending with the -1 entries last
@@ -148,7 +149,7 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
  *   [r * rows_per_src, (r+1) * rows_per_src) with the kv token stride), which may be other
  *   GPUs' memory mapped by dsalt_ipc_open (plain NVLink loads), gathered once per call into
  *   the workspace as 128-row tiles. q_pos0 and q_rows are multiples of 128 (and of
- *   lmk_block); bf16 / fp16 inputs; head_dim 64.
+ *   lmk_block); bf16 / fp16 inputs; head_dim 64 or 128.
  * dsalt_ipc_export / dsalt_ipc_open / dsalt_ipc_close: CUDA IPC handles (64 bytes) of a
  *   device pointer inside an allocation, for the peer tables above.
  */
