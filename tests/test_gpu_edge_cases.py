@@ -162,3 +162,36 @@ def test_signals_bulk_and_fallback_paths(ops, d_model, n_kv, head_dim, T):
     np.testing.assert_array_equal(xn.cpu().numpy(), O.row_norms(x.float().numpy(), None))
     np.testing.assert_array_equal(vn.cpu().numpy(),
                                   O.row_norms(v.float().numpy().reshape(T, n_kv, head_dim), None))
+
+
+@pytest.mark.parametrize("gate_scale", [0.05, 0.0])
+def test_signals_rows_outside_the_fast_range(ops, gate_scale):
+    """Rows whose squares or gate products would underflow or overflow in fp32, zero rows,
+    a single tiny element and a zero gate: the kernel's exact sums must not pass through
+    fp32 intermediates, so widths, logits and norms stay bit-exact with the oracle's
+    float64 sums (an overflowing norm is inf on both sides)."""
+    g0 = torch.Generator().manual_seed(11)
+    T, d_model, n_kv, head_dim = 640, 1024, 16, 64
+    x = torch.randn(T, d_model, generator=g0)
+    v = torch.randn(T, n_kv * head_dim, generator=g0)
+    x[0] = 0.0
+    x[1] *= 2.0 ** -70  # squares underflow fp32
+    x[2] *= 2.0 ** 70  # squares overflow fp32 (norm inf)
+    x[3, 5] = 2.0 ** -100  # one tiny element among normal ones
+    x[4, :512] = 0.0
+    v[0] = 0.0
+    v[1, :64] *= 2.0 ** -70  # one value head underflows
+    v[2, 64:128] *= 2.0 ** 66  # one value head overflows
+    x, v = x.bfloat16(), v.bfloat16()
+    gw = (gate_scale * torch.randn(d_model, generator=g0)).bfloat16()
+    gb = torch.tensor([0.1]).bfloat16()
+    for rnd in (False, True):
+        w, xn, vn, lg = ops.window_signals(x.to(_dev()), gw.to(_dev()), gb.to(_dev()), 16, 512, v.to(_dev()),
+                                           head_dim, rnd, return_logit=True)
+        lo = O.window_logit(x.float().numpy(), gw.float().numpy(), float(gb.float()[0]), "bf16")
+        np.testing.assert_array_equal(lg.cpu().numpy(), lo)
+        wo, amb = O.window_sizes_from_logit(lo, 16, 512, "bf16")
+        assert not ((w.cpu().numpy() != wo) & ~amb).any()
+        np.testing.assert_array_equal(xn.cpu().numpy(), O.row_norms(x.float().numpy(), "bf16" if rnd else None))
+        np.testing.assert_array_equal(
+            vn.cpu().numpy(), O.row_norms(v.float().numpy().reshape(T, n_kv, head_dim), "bf16" if rnd else None))
