@@ -21,6 +21,7 @@ step time.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -85,8 +86,9 @@ class ClockSampler:
     collects one line per 10 ms; entering waits (up to 3 s) for the first sample, so that
     sampling is running before the timed region starts, and leaving takes one more."""
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, index, interval_ms=10):
+        self.index = index  # None: every GPU of the node, one line per GPU and interval
+        self.interval_ms = interval_ms
         self.proc = None
         self.lines = []
 
@@ -98,12 +100,13 @@ class ClockSampler:
     def __enter__(self):
         import threading
         try:
+            sel = [] if self.index is None else ["-i", str(self.index)]
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index),
+                ["nvidia-smi", *sel,
                  "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                  "clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "10"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -326,24 +329,30 @@ def run_sharded(args, rank, world, local, dev):
     del x, q
     torch.cuda.synchronize()
 
-    # the step is ~25 launches: captured once into a CUDA graph (a Python host issues them
-    # more slowly than the GPUs run them at small shards)
-    core.capture(xs, gw, gb, alpha, qs)
+    # the step is ~25 launches: captured into CUDA graphs of one and of GRAPH_STEPS steps (a
+    # Python host issues launches more slowly than the GPUs run them at small shards, and
+    # eight ranks share the host's cores); the timed loop replays the multi-step graph and
+    # reads the device status word once, after the loop
+    GRAPH_STEPS = 4
+    core.capture(xs, gw, gb, alpha, qs, steps=1)
+    core.capture(xs, gw, gb, alpha, qs, steps=GRAPH_STEPS)
 
-    def step():
-        core.replay()
+    def steps(n):
+        for _ in range(n // GRAPH_STEPS):
+            core.replay(GRAPH_STEPS, read_status=False)
+        for _ in range(n % GRAPH_STEPS):
+            core.replay(1, read_status=False)
 
-    for _ in range(args.warmup):
-        step()
+    steps(args.warmup)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    # one nvidia-smi (rank 0) samples every GPU of the node
+    with (ClockSampler(None, 20) if rank == 0 else contextlib.nullcontext()) as clk:
         e0.record(stream)
-        for _ in range(args.steps):
-            step()
+        steps(args.steps)
         e1.record(stream)
         torch.cuda.synchronize()
     barrier(world)

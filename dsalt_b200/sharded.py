@@ -184,6 +184,7 @@ class ShardedCore:
         self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self._status_event = None
         self._graph, self._graph_res = None, None
+        self._graphs = {}  # steps per graph -> (graph, outputs of its last step)
 
     def _open_peers(self):
         """Peer pointer tables (CUDA IPC; own entries local): K / V shards, the signal
@@ -215,7 +216,8 @@ class ShardedCore:
         self._ws_peers = torch.tensor(tables[6], dtype=torch.int64, device=dev)
 
     def close(self):
-        self._graph = None  # the graph's kernels hold peer pointers: release it first
+        # the graphs' kernels hold peer pointers: release them first
+        self._graph, self._graph_res, self._graphs = None, None, {}
         for ptr, off in self._peers:
             self.ops.ipc_close(ptr, off)
         self._peers = []
@@ -271,30 +273,43 @@ class ShardedCore:
             self._status_event = torch.cuda.Event()
         self._status_event.record()
 
-    def capture(self, x, gate_weight, gate_bias, alpha, q):
-        """Record one step into a CUDA graph (peer exchange only): the step is ~25 launches,
-        which a Python host issues more slowly than the GPUs run them once the shards are
-        small. The graph keeps the pointers of ``x``, ``q``, ``k_local`` / ``v_local`` and of
+    def capture(self, x, gate_weight, gate_bias, alpha, q, steps: int = 1):
+        """Record ``steps`` consecutive steps into one CUDA graph (peer exchange only): a step
+        is ~25 launches, which a Python host issues more slowly than the GPUs run them once
+        the shards are small, and with several steps per graph one host call queues several
+        steps. The graph keeps the pointers of ``x``, ``q``, ``k_local`` / ``v_local`` and of
         the weights: write new inputs into those tensors and call :meth:`replay`. Every rank
-        captures together (the capture runs one ordinary step first, with its barriers)."""
+        captures together (the capture runs one ordinary step first, with its barriers).
+        Capturing again keeps the graphs captured before (see :meth:`replay`)."""
         if self.exchange != "peer":
             raise ValueError("graph capture needs exchange='peer'")
+        if steps < 1:
+            raise ValueError("steps must be >= 1")
         self.forward(x, gate_weight, gate_bias, alpha, q)  # first-call set-up outside the capture
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         # library set-up calls made outside the stream (function attributes, device queries)
         # are allowed during the capture
         with torch.cuda.graph(g, capture_error_mode="thread_local"):
-            res = self._step(x, gate_weight, gate_bias, alpha, q)
+            for _ in range(steps):
+                res = self._step(x, gate_weight, gate_bias, alpha, q)
+        self._graphs[steps] = (g, res)
         self._graph, self._graph_res = g, res
 
-    def replay(self):
-        """One step from the captured graph; returns (out, landmark sets) like :meth:`forward`."""
+    def replay(self, steps: int = 1, read_status: bool = True):
+        """``steps`` steps from the graph captured with that many steps (default: one);
+        returns (out, landmark sets) of the last one like :meth:`forward`. With
+        ``read_status=False`` the device status word is not read after the replay (a timed
+        loop reads it once at its end with :meth:`check`-like calls of its own)."""
         if self._status_event is not None and self._status_event.query():
             self._raise_if_failed()
-        self._graph.replay()
-        self._read_status()
-        return self._graph_res
+        if steps not in self._graphs:
+            raise ValueError(f"no graph of {steps} steps captured")
+        g, res = self._graphs[steps]
+        g.replay()
+        if read_status:
+            self._read_status()
+        return res
 
     def _step(self, x, gate_weight, gate_bias, alpha, q, events=None):
         ops, p = self.ops, self.plan
