@@ -114,6 +114,9 @@ class DSALTTransformerBlock(nn.Module):
         self.attn = DSALTAttention(d_model, n_heads, n_min, n_max, k_lmk, max_seq_len, dropout=dropout,
                                    yarn_scale=yarn_scale, layer_idx=layer_idx, n_kv_heads=n_kv_heads,
                                    qkv_bias=qkv_bias, rope_base=rope_base, selection=selection, block=block)
+        # the dense [H, T0, T0] _last_P rebuild is off in the decoder stack: at prefill lengths it
+        # does not fit (set attn._collect_last_P = True on a layer whose metrics are wanted)
+        self.attn._collect_last_P = False
         self.ffn = SwiGLUFFN(d_model, d_ff, dropout)
 
     def forward(self, x, cu_seqlens=None, max_seqlen=None, gradient_checkpointing=False, rope_cs=None, cu_list=None):

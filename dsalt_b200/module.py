@@ -12,8 +12,14 @@ are indexed by the kernels instead of being repeated (``_repeat_kv``, ``:254-268
 ``selection="block_causal"`` selects per ``block`` queries from earlier positions only,
 as ``results/causal_landmark_check.py``'s ``"block"`` mode does.
 
-Out of scope (raise): the training path, the batched ``[B, T, d]`` path, and the dense
-``_last_P`` rebuild (``:636-704``); ``_collect_last_P`` defaults to False here.
+In eval mode ``_last_P`` holds the dense attention matrix ``[H, T0, T0]`` of the first
+packed sequence, rebuilt as the reference does for its analysis metrics (``:636-704``:
+landmarks of that sequence alone by ``compute_landmark_indices``, the window ∪ landmark
+mask, softmax of the masked scores in the caller's dtype). As in the reference it is
+collected unless ``_collect_last_P`` is set to False; it costs O(T0²) memory, so callers
+that need only the output (the decoder stack in :mod:`dsalt_b200.model`) turn it off.
+
+Out of scope (raise): the training path and the batched ``[B, T, d]`` path.
 """
 from __future__ import annotations
 
@@ -77,7 +83,7 @@ class DSALTAttention(nn.Module):
         self.alpha_w = nn.Parameter(torch.full((n_heads,), math.log(0.6 / 0.4)))
         self.tau_win, self.tau_lmk, self.win_edge = 1.0, 2.0, 4
         self._last_P = None
-        self._collect_last_P = False
+        self._collect_last_P = True  # the reference's default (dsalt_attention.py:639)
         cos, sin = build_rope_cache(max_seq_len, self.head_dim, torch.device("cpu"), base=rope_base, scale=yarn_scale)
         self.register_buffer("rope_cos", cos, persistent=False)
         self.register_buffer("rope_sin", sin, persistent=False)
@@ -95,8 +101,6 @@ class DSALTAttention(nn.Module):
             raise NotImplementedError("dsalt_b200 implements the packed path; pass cu_seqlens")
         if self.training:
             raise NotImplementedError("dsalt_b200 implements the inference forward; call .eval()")
-        if self._collect_last_P:
-            raise NotImplementedError("the dense _last_P rebuild is not part of dsalt_b200")
         return self._packed(x, cu_seqlens, x.shape[0], x.device, rope_cs, cu_list)
 
     @torch.no_grad()
@@ -131,6 +135,32 @@ class DSALTAttention(nn.Module):
                                                     cu_h)
         out = torch.ops.dsalt_b200.dsalt_attention(q.contiguous(), k.contiguous(), v.contiguous(), lmk, None, w,
                                                    cu_seqlens, 0 if mode == "global" else self.block, cu_h, q.dtype)
-        self._last_P = None
+        self._last_P = self._rebuild_last_P(x, q, k, w, alpha, cu_h) if self._collect_last_P else None
         aux = torch.zeros((), device=x.device, dtype=x.dtype)
         return self.out_proj(out.view(T, self.d_model).to(self.out_proj.weight.dtype)), aux
+
+    @torch.no_grad()
+    def _rebuild_last_P(self, x, q, k, w, alpha, cu_h):
+        """Dense attention ``[H, T0, T0]`` of the first sequence (``dsalt_attention.py:643-702``):
+        its landmarks selected on that sequence alone, query ``i`` attending to its window
+        ``[i - w(i) + 1, i]`` and to every landmark ``j <= i``, softmax of the masked scaled
+        scores. ``q`` / ``k`` are the post-RoPE projections in the compute dtype."""
+        s0, e0 = int(cu_h[0]), int(cu_h[1])
+        T0, H, dev = e0 - s0, self.n_heads, x.device
+        q0 = q[s0:e0].transpose(0, 1)
+        k0 = k[s0:e0].repeat_interleave(self.n_rep, dim=1).transpose(0, 1)
+        w0 = w[s0:e0]
+        cu0 = torch.tensor([0, T0], dtype=torch.int32, device=dev)
+        lmk_idx, _, _ = ops.compute_landmark_indices(x[s0:e0].float(), self.v_proj.weight.float(), alpha.float(), w0,
+                                                     cu0, self.k_lmk, self.n_min, T0, [0, T0],
+                                                     head_dim=self.head_dim)
+        rows = torch.arange(T0, device=dev)
+        causal = rows.unsqueeze(0) <= rows.unsqueeze(1)                          # key j <= query i
+        in_win = (rows.unsqueeze(0) >= rows.unsqueeze(1) - w0.long().unsqueeze(1) + 1) & causal
+        lmk0 = lmk_idx[:, 0, :]                                                  # [H, k], -1 padded
+        col_is_lmk = torch.zeros(H, T0 + 1, dtype=torch.bool, device=dev)
+        col_is_lmk.scatter_(1, torch.where(lmk0 >= 0, lmk0, T0), True)          # -1 slots land in column T0
+        full_mask = in_win.unsqueeze(0) | (col_is_lmk[:, :T0].unsqueeze(1) & causal.unsqueeze(0))
+        sc = torch.matmul(q0, k0.transpose(-2, -1)) * (1.0 / math.sqrt(self.head_dim))
+        additive = sc.new_full((H, T0, T0), float("-inf")).masked_fill_(full_mask, 0.0)
+        return torch.softmax(sc + additive, dim=-1).detach()

@@ -230,6 +230,67 @@ def test_attention_gqa_fp16_and_bias(ops):
 
 
 # --------------------------------------------------------------------------- module vs reference fixtures
+@pytest.mark.parametrize("n_kv", [4, 2])
+def test_module_last_P_rebuild(n_kv):
+    """``_last_P`` (dense attention of the first sequence, ``dsalt_attention.py:636-704``):
+    landmarks of that sequence alone (oracle ``select_global`` on the same signals), the
+    window ∪ causal-landmark mask and the softmax of the scaled scores, against a float64
+    restatement; fp32 module, so the tolerance is that of one fp32 GEMM and softmax."""
+    from dsalt_b200 import DSALTAttention, ops
+    dev = _dev()
+    torch.manual_seed(5)
+    dm, H, n_min, n_max, k = 256, 4, 16, 96, 24
+    D = dm // H
+    cu = [0, 300, 520]
+    mod = DSALTAttention(dm, H, n_min, n_max, k, 640, n_kv_heads=n_kv).to(dev).eval()
+    with torch.no_grad():
+        for name, prm in mod.named_parameters():
+            if name != "alpha_w":
+                prm.normal_(0.0, 0.02)
+    assert mod._collect_last_P  # the reference's default
+    x = torch.randn(cu[-1], dm, device=dev)
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    mod(x, cu_t, cu_list=cu)
+    P = mod._last_P
+    T0 = cu[1]
+    assert P.shape == (H, T0, T0) and P.dtype == torch.float32
+    with torch.no_grad():
+        x0 = x[:T0]
+        logit = mod.win_gate(x0).squeeze(-1)
+        w_or, amb = O.window_sizes_from_logit(logit.cpu().numpy(), n_min, n_max, "f32")
+        w, _, _ = ops.window_signals(x0, mod.win_gate.weight.view(-1), mod.win_gate.bias, n_min, n_max,
+                                     x0 @ mod.v_proj.weight.T, D, False, logit=logit)
+        w = w.cpu().numpy()
+        assert ((w == w_or) | amb).all()
+        v0 = (x0.float() @ mod.v_proj.weight.float().T).cpu().numpy()
+        xn, vn = O.token_signals(x0.cpu().numpy(), v0, n_kv, D, None)
+        alpha = torch.sigmoid(mod.alpha_w).cpu().numpy()
+        lmk, *_ = O.select_global(xn, vn, alpha, w, [0, T0], k, H)
+        cos, sin = C.rope_cache(T0, D)
+        q = mod.q_proj(x0).view(T0, H, D).cpu()
+        kk = mod.k_proj(x0).view(T0, n_kv, D).cpu()
+        q, kk = C.rope(q, kk, cos.unsqueeze(1), sin.unsqueeze(1))
+        kk = kk.repeat_interleave(H // n_kv, dim=1)
+    qd = q.double().numpy().transpose(1, 0, 2)
+    kd = kk.double().numpy().transpose(1, 0, 2)
+    sc = qd @ kd.transpose(0, 2, 1) / math.sqrt(D)
+    i = np.arange(T0)
+    causal = i[None, :] <= i[:, None]
+    mask = np.broadcast_to((i[None, :] >= i[:, None] - w[:, None] + 1) & causal, (H, T0, T0)).copy()
+    for h in range(H):
+        pos = lmk[h, 0][lmk[h, 0] >= 0]
+        col = np.zeros(T0, dtype=bool)
+        col[pos] = True
+        mask[h] |= col[None, :] & causal
+    sc = np.where(mask, sc, -np.inf)
+    e = np.exp(sc - sc.max(-1, keepdims=True))
+    ref = e / e.sum(-1, keepdims=True)
+    np.testing.assert_allclose(P.cpu().numpy(), ref, atol=1e-5, rtol=0)
+    # the landmark columns the rebuild used are the oracle's: a position p outside row i's
+    # window carries mass exactly when p is one of the head's landmarks (and p <= i)
+    assert np.array_equal(P.cpu().numpy() > 0, mask)
+
+
 @pytest.mark.parametrize("name", ["cfg1_fp32", "cfg2_bf16_packed", "cfg4_block", "gqa_block"])
 def test_module_matches_reference_fixture(name):
     from dsalt_b200 import DSALTAttention
