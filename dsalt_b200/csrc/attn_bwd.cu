@@ -1,0 +1,345 @@
+// Backward of the sparse attention forward (reference: dsalt/kernels/dsalt_triton_bwd.py).
+//
+// Gradients of out = softmax(logits over A(i)) · V with A(i) = the window
+// [max(0, i−w(i)+1), i] and the landmarks p of the row's set with 0 ≤ p < L, p ≤ i and
+// p < i−w(i)+1, logits q·k·scale (+ landmark bias). As the reference (:18-212): the forward's
+// log-sum-exp is reused, P is recomputed, delta = Σ_d O·dO, dS = P ⊙ (dO·Vᵀ − delta) · scale,
+// dQ = dS·K, dK += dSᵀ·Q, dV += Pᵀ·dO (atomic adds: a key belongs to many query tiles),
+// d_bias[h, set, slot] += Σ_i P (dO·v − delta). Rows whose log-sum-exp is −inf contribute
+// nothing. Grouped kv heads: head h uses kv head h / (H / H_kv) and its kv gradients add into
+// that head.
+//
+// CUDA cores, fp32 throughout. One CTA per (64-query tile, head), 256 threads; the key axis is
+// walked in 32-key tiles: the window band of the tile, then the landmark slots of its set.
+// Per key tile the Q/dO tile (resident), the K/V tile and the P/dS tile sit in shared memory
+// with padded rows (stride HD + 1 floats: the 32 banks see distinct rows).
+#include "common.cuh"
+
+namespace dsalt {
+
+int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream);
+
+namespace bwd {
+
+constexpr int BM = 64;        // queries per CTA
+constexpr int BN = 32;        // keys per tile
+constexpr int THREADS = 256;
+
+template <int HD>
+struct Smem {
+  static constexpr int LD = HD + 1;  // padded row stride (floats)
+  static constexpr int Q_OFF = 0, DO_OFF = BM * LD, K_OFF = 2 * BM * LD, V_OFF = K_OFF + BN * LD;
+  static constexpr int P_OFF = V_OFF + BN * LD, DS_OFF = P_OFF + BM * (BN + 1);
+  static constexpr int FLOATS = DS_OFF + BM * (BN + 1);
+  static constexpr size_t BYTES = (size_t)FLOATS * 4 + BM * 16 + BN * 8;  // + per-row and per-key ints
+};
+
+struct Params {
+  const void* q;
+  const void* k;
+  const void* v;
+  int dtype;
+  int H, Hkv;
+  int64_t q_stride, kv_stride;  // elements between consecutive tokens
+  const void* out;
+  int out_dtype;
+  const void* dout;
+  int dout_dtype;
+  const float* lse;  // [T, H], natural log
+  const int32_t* w;
+  const int32_t* lmk;
+  const float* lmk_bias;
+  int k_lmk, lmk_block;
+  const int32_t* cu;
+  int n_seqs;
+  const int32_t* tile_base;  // per sequence: first 64-query tile
+  const int32_t* set_base;   // per sequence: first landmark set (block mode)
+  float scale;
+  float* dq;      // [T, H, HD]
+  float* dk;      // [T, Hkv, HD]
+  float* dv;      // [T, Hkv, HD]
+  float* d_bias;  // [H, n_sets, k] or null
+};
+
+template <int HD>
+__global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
+  using SM = Smem<HD>;
+  constexpr int LD = SM::LD;
+  extern __shared__ float sm[];
+  float* sq = sm + SM::Q_OFF;
+  float* sdo = sm + SM::DO_OFF;
+  float* sk = sm + SM::K_OFF;
+  float* sv = sm + SM::V_OFF;
+  float* sp = sm + SM::P_OFF;   // [BM][BN + 1]
+  float* sds = sm + SM::DS_OFF;  // [BM][BN + 1]
+  int* row_lo = reinterpret_cast<int*>(sm + SM::FLOATS);  // per row: window start (raw, may be < 0)
+  int* row_ok = row_lo + BM;                                // per row: valid and finite lse
+  float* row_lse = reinterpret_cast<float*>(row_ok + BM);
+  float* row_delta = row_lse + BM;
+  int* key_pos = reinterpret_cast<int*>(row_delta + BM);    // per key of the tile: position or -1
+  int* key_slot = key_pos + BN;                             // landmark slot (or -1 for window keys)
+
+  const int tile = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  if (tile >= p.tile_base[p.n_seqs]) return;
+  int lo_s = 0, hi_s = p.n_seqs;  // sequence of this tile
+  while (hi_s - lo_s > 1) {
+    const int mid = (lo_s + hi_s) >> 1;
+    if (p.tile_base[mid] <= tile) lo_s = mid;
+    else hi_s = mid;
+  }
+  const int s = lo_s;
+  const int seq0 = p.cu[s], L = p.cu[s + 1] - seq0;
+  const int m0 = (tile - p.tile_base[s]) * BM;
+  const int hk = h / (p.H / p.Hkv);
+  const int set = p.lmk_block > 0 ? p.set_base[s] + m0 / p.lmk_block : s;
+  const int n_sets = p.lmk_block > 0 ? p.set_base[p.n_seqs] : p.n_seqs;
+
+  // resident Q and dO tiles (fp32), per-row window start, lse and delta = Σ O·dO
+  for (int e = tid; e < BM * HD; e += THREADS) {
+    const int r = e / HD, d = e - r * HD;
+    const int i = m0 + r;
+    float qv = 0.f, dov = 0.f;
+    if (i < L) {
+      const int64_t t = seq0 + i;
+      qv = load_elem(p.q, t * p.q_stride + (int64_t)h * HD + d, p.dtype);
+      dov = load_elem(p.dout, (t * p.H + h) * HD + d, p.dout_dtype);
+    }
+    sq[r * LD + d] = qv;
+    sdo[r * LD + d] = dov;
+  }
+  {
+    const int r = tid >> 2, part = tid & 3;  // 4 threads per row
+    const int i = m0 + r;
+    float acc = 0.f;
+    if (i < L) {
+      const int64_t t = seq0 + i;
+      for (int d = part; d < HD; d += 4)
+        acc += load_elem(p.out, (t * p.H + h) * HD + d, p.out_dtype) * load_elem(p.dout, (t * p.H + h) * HD + d,
+                                                                               p.dout_dtype);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (part == 0) {
+      float l = -INFINITY;
+      int lo = 0x3fffffff;
+      if (i < L) {
+        const int64_t t = seq0 + i;
+        l = p.lse[t * p.H + h];
+        lo = i - max(p.w[t], 1) + 1;
+      }
+      row_delta[r] = acc;
+      row_lse[r] = l;
+      row_lo[r] = lo;
+      row_ok[r] = (i < L) && (l > -INFINITY);
+    }
+  }
+  __syncthreads();
+  int wmin_lo = 0x3fffffff;
+  for (int r = 0; r < BM; ++r)
+    if (row_ok[r]) wmin_lo = min(wmin_lo, max(row_lo[r], 0));
+  const int i_last = min(m0 + BM, L) - 1;
+  const int n_wt = wmin_lo > i_last ? 0 : (i_last - (wmin_lo & ~(BN - 1))) / BN + 1;  // window tiles
+  const int kw0 = wmin_lo & ~(BN - 1);
+  const int n_lt = (p.k_lmk + BN - 1) / BN;
+  const int32_t* P = p.lmk + ((int64_t)h * n_sets + set) * p.k_lmk;
+  const float* Bset = p.lmk_bias ? p.lmk_bias + ((int64_t)h * n_sets + set) * p.k_lmk : nullptr;
+
+  // this thread's share of dQ: row tid >> 2, dims (tid & 3) + 4 m
+  float dq_acc[HD / 4];
+#pragma unroll
+  for (int m = 0; m < HD / 4; ++m) dq_acc[m] = 0.f;
+
+  for (int kt = 0; kt < n_wt + n_lt; ++kt) {
+    const bool is_w = kt < n_wt;
+    const int lt = kt - n_wt;
+    if (tid < BN) {
+      int pos = -1, slot = -1;
+      if (is_w) {
+        const int j = kw0 + kt * BN + tid;
+        pos = (j >= 0 && j < L) ? j : -1;
+      } else {
+        slot = lt * BN + tid;
+        const int pp = slot < p.k_lmk ? P[slot] : -1;
+        pos = (pp >= 0 && pp < L) ? pp : -1;
+        if (slot >= p.k_lmk) slot = -1;
+      }
+      key_pos[tid] = pos;
+      key_slot[tid] = slot;
+    }
+    __syncthreads();
+    for (int e = tid; e < BN * HD; e += THREADS) {
+      const int c = e / HD, d = e - c * HD;
+      const int pos = key_pos[c];
+      float kv = 0.f, vv = 0.f;
+      if (pos >= 0) {
+        const int64_t off = (seq0 + pos) * p.kv_stride + (int64_t)hk * HD + d;
+        kv = load_elem(p.k, off, p.dtype);
+        vv = load_elem(p.v, off, p.dtype);
+      }
+      sk[c * LD + d] = kv;
+      sv[c * LD + d] = vv;
+    }
+    __syncthreads();
+    // P and dS: thread -> row tid >> 2, columns (tid & 3) + 4 j
+    {
+      const int r = tid >> 2, c0 = tid & 3;
+      float sacc[BN / 4], dpacc[BN / 4];
+#pragma unroll
+      for (int j = 0; j < BN / 4; ++j) sacc[j] = dpacc[j] = 0.f;
+      const float* qr = sq + r * LD;
+      const float* dor = sdo + r * LD;
+#pragma unroll 4
+      for (int d = 0; d < HD; ++d) {
+        const float a = qr[d], b = dor[d];
+#pragma unroll
+        for (int j = 0; j < BN / 4; ++j) {
+          const int c = c0 + 4 * j;
+          sacc[j] = fmaf(a, sk[c * LD + d], sacc[j]);
+          dpacc[j] = fmaf(b, sv[c * LD + d], dpacc[j]);
+        }
+      }
+      const int i = m0 + r;
+      const bool ok = row_ok[r];
+      const int lo = row_lo[r];
+      const float l = row_lse[r], dl = row_delta[r];
+#pragma unroll
+      for (int j = 0; j < BN / 4; ++j) {
+        const int c = c0 + 4 * j;
+        const int pos = key_pos[c];
+        bool valid = ok && pos >= 0;
+        float logit = sacc[j] * p.scale;
+        if (is_w) {
+          valid = valid && pos >= lo && pos <= i;
+        } else {
+          valid = valid && pos <= i && pos < lo;
+          if (valid && Bset) logit += Bset[key_slot[c]];
+        }
+        const float pr = valid ? expf(logit - l) : 0.f;
+        const float rec = pr * (dpacc[j] - dl);
+        sp[r * (BN + 1) + c] = pr;
+        sds[r * (BN + 1) + c] = rec;  // scaled below where dS is used
+      }
+    }
+    __syncthreads();
+    // dQ += dS · K (dS = rec · scale)
+    {
+      const int r = tid >> 2, d0 = tid & 3;
+      const float* dsr = sds + r * (BN + 1);
+#pragma unroll 4
+      for (int c = 0; c < BN; ++c) {
+        const float ds = dsr[c] * p.scale;
+#pragma unroll
+        for (int m = 0; m < HD / 4; ++m) dq_acc[m] = fmaf(ds, sk[c * LD + d0 + 4 * m], dq_acc[m]);
+      }
+    }
+    // dK_tile = dSᵀ · Q, dV_tile = Pᵀ · dO: thread -> key tid >> 3, dims (tid & 7) + 8 m
+    {
+      const int c = tid >> 3, d0 = tid & 7;
+      constexpr int ND = HD / 8;
+      float dkacc[ND], dvacc[ND];
+#pragma unroll
+      for (int m = 0; m < ND; ++m) dkacc[m] = dvacc[m] = 0.f;
+#pragma unroll 4
+      for (int r = 0; r < BM; ++r) {
+        const float ds = sds[r * (BN + 1) + c] * p.scale, pr = sp[r * (BN + 1) + c];
+#pragma unroll
+        for (int m = 0; m < ND; ++m) {
+          dkacc[m] = fmaf(ds, sq[r * LD + d0 + 8 * m], dkacc[m]);
+          dvacc[m] = fmaf(pr, sdo[r * LD + d0 + 8 * m], dvacc[m]);
+        }
+      }
+      const int pos = key_pos[c];
+      if (pos >= 0) {
+        float* gk = p.dk + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
+        float* gv = p.dv + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
+#pragma unroll
+        for (int m = 0; m < ND; ++m) {
+          if (dkacc[m] != 0.f) atomicAdd(gk + d0 + 8 * m, dkacc[m]);
+          if (dvacc[m] != 0.f) atomicAdd(gv + d0 + 8 * m, dvacc[m]);
+        }
+      }
+    }
+    // landmark bias gradient: Σ_i P (dO·v − delta) per slot
+    if (!is_w && p.d_bias != nullptr && tid < BN) {
+      float acc = 0.f;
+      for (int r = 0; r < BM; ++r) acc += sds[r * (BN + 1) + tid];
+      const int slot = key_slot[tid];
+      if (slot >= 0 && acc != 0.f) atomicAdd(p.d_bias + ((int64_t)h * n_sets + set) * p.k_lmk + slot, acc);
+    }
+    __syncthreads();
+  }
+  // dQ of this thread's row and dims
+  {
+    const int r = tid >> 2, d0 = tid & 3;
+    const int i = m0 + r;
+    if (i < L) {
+      float* g = p.dq + ((seq0 + i) * (int64_t)p.H + h) * HD;
+#pragma unroll
+      for (int m = 0; m < HD / 4; ++m) g[d0 + 4 * m] = dq_acc[m];
+    }
+  }
+}
+
+}  // namespace bwd
+
+// two per-sequence tables of n_seqs + 1 ints (64-query tiles, landmark sets), 256-byte aligned
+size_t attention_bwd_workspace_bytes(int n_seqs) { return 2 * ((((size_t)n_seqs + 1) * 4 + 255) / 256 * 256); }
+
+int launch_attn_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int HD,
+                    int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype, const void* dout,
+                    int dout_dtype, const float* lse, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
+                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, float* dq, float* dk, float* dv,
+                    float* d_bias, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  using namespace bwd;
+  if (HD != 64 && HD != 128) return fail(DSALT_ERR_UNSUPPORTED, "attention backward: head_dim %d (64, 128)", HD);
+  if (H < 1 || Hkv < 1 || H % Hkv) return fail(DSALT_ERR_INVALID, "attention backward: heads %d / kv heads %d", H, Hkv);
+  if (lmk_block > 0 && lmk_block % BM)
+    return fail(DSALT_ERR_UNSUPPORTED, "attention backward: lmk_block must be a multiple of %d", BM);
+  if (ws_bytes < attention_bwd_workspace_bytes(n_seqs))
+    return fail(DSALT_ERR_WORKSPACE, "attention backward: workspace %zu < %zu", ws_bytes,
+                attention_bwd_workspace_bytes(n_seqs));
+  if (T == 0 || n_seqs == 0) return DSALT_OK;
+  int32_t* tile_base = reinterpret_cast<int32_t*>(workspace);
+  int32_t* set_base = tile_base + ((n_seqs + 1 + 63) / 64) * 64;
+  int rc;
+  if ((rc = launch_chunk_table(cu, n_seqs, BM, tile_base, stream))) return rc;
+  if (lmk_block > 0 && (rc = launch_chunk_table(cu, n_seqs, lmk_block, set_base, stream))) return rc;
+  Params p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.dtype = dtype;
+  p.H = H;
+  p.Hkv = Hkv;
+  p.q_stride = q_stride;
+  p.kv_stride = kv_stride;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.dout = dout;
+  p.dout_dtype = dout_dtype;
+  p.lse = lse;
+  p.w = w;
+  p.lmk = lmk;
+  p.lmk_bias = lmk_bias;
+  p.k_lmk = k_lmk;
+  p.lmk_block = lmk_block;
+  p.cu = cu;
+  p.n_seqs = n_seqs;
+  p.tile_base = tile_base;
+  p.set_base = set_base;
+  p.scale = (float)(1.0 / sqrt((double)HD));
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.d_bias = d_bias;
+  const int64_t max_tiles = T / BM + n_seqs;
+  auto kern = HD == 64 ? attn_bwd_kernel<64> : attn_bwd_kernel<128>;
+  const size_t smem = HD == 64 ? Smem<64>::BYTES : Smem<128>::BYTES;
+  if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                       "attention backward smem attr")))
+    return rc;
+  kern<<<dim3((unsigned)max_tiles, (unsigned)H), THREADS, smem, stream>>>(p);
+  return check_cuda(cudaGetLastError(), "attention backward launch");
+}
+
+}  // namespace dsalt

@@ -41,6 +41,12 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
                    int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
                    cudaStream_t stream, const ShardArgs* shard = nullptr);
 int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream);
+size_t attention_bwd_workspace_bytes(int n_seqs);
+int launch_attn_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int HD,
+                    int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype, const void* dout,
+                    int dout_dtype, const float* lse, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
+                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, float* dq, float* dk, float* dv,
+                    float* d_bias, void* workspace, size_t ws_bytes, cudaStream_t stream);
 int launch_peer_barrier(int* own_flag, const int* const* flags, int n_ranks, int rank, int epoch, int* err,
                         cudaStream_t stream);
 int launch_peer_allgather(void* dst, const void* const* src, int n_ranks, int rank, int64_t bytes_per_rank,
@@ -211,6 +217,44 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
   return launch_attn_tc(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
                         lmk_block, cu_seqlens, n_seqs, set_base, tile_base, plan, attention_max_tiles(T, n_seqs), out,
                         out_dtype, lse, device_status_ptr(), s);
+}
+
+size_t dsalt_attention_bwd_workspace_bytes(int64_t T, int n_seqs) {
+  if (n_seqs < 1 || T < 0) return 0;
+  return attention_bwd_workspace_bytes(n_seqs);
+}
+
+int dsalt_attention_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
+                        int head_dim, int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype,
+                        const void* dout, int dout_dtype, const float* lse, const int32_t* w, const int32_t* lmk,
+                        const float* lmk_bias, int k_lmk, int lmk_block, int n_sets, const int32_t* cu_seqlens,
+                        int n_seqs, float* dq, float* dk, float* dv, float* d_bias, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (T < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || head_dim < 1 || n_seqs < 1 || k_lmk < 0 ||
+      lmk_block < 0 || n_sets < 0)
+    return fail(DSALT_ERR_INVALID, "attention backward: bad sizes");
+  if (!valid_dtype(dtype) || !valid_dtype(out_dtype) || !valid_dtype(dout_dtype))
+    return fail(DSALT_ERR_INVALID, "attention backward: dtype");
+  if (q_stride < (int64_t)n_heads * head_dim || kv_stride < (int64_t)n_kv * head_dim)
+    return fail(DSALT_ERR_INVALID, "attention backward: token stride smaller than heads x head_dim");
+  if (T == 0) return DSALT_OK;
+  if (!q || !k || !v || !out || !dout || !lse || !w || !cu_seqlens || !dq || !dk || !dv || (k_lmk > 0 && !lmk) ||
+      !workspace)
+    return fail(DSALT_ERR_INVALID, "attention backward: null pointer");
+  if (T > 0x7fffff00LL) return fail(DSALT_ERR_UNSUPPORTED, "attention backward: T too large");
+  // dk, dv and d_bias are sums over query tiles (atomic adds): cleared here, in stream order
+  int rc;
+  if ((rc = check_cuda(cudaMemsetAsync(dk, 0, sizeof(float) * (size_t)T * n_kv * head_dim, s), "clear dk")) ||
+      (rc = check_cuda(cudaMemsetAsync(dv, 0, sizeof(float) * (size_t)T * n_kv * head_dim, s), "clear dv")))
+    return rc;
+  if (d_bias != nullptr && k_lmk > 0 &&
+      (rc = check_cuda(cudaMemsetAsync(d_bias, 0, sizeof(float) * (size_t)n_heads * n_sets * k_lmk, s),
+                       "clear d_bias")))
+    return rc;
+  return launch_attn_bwd(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, out, out_dtype, dout,
+                         dout_dtype, lse, w, lmk, lmk_bias, k_lmk, lmk_block, cu_seqlens, n_seqs, dq, dk, dv, d_bias,
+                         workspace, workspace_bytes, s);
 }
 
 size_t dsalt_select_block_range_workspace_bytes(int64_t seq_len, int n_heads, int n_kv, int k, int block,

@@ -241,6 +241,79 @@ def dsalt_attention(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, *, lmk_
     return (out, lse) if return_lse else out
 
 
+def dsalt_attention_backward(grad_out, q, k, v, out, lse, lmk_indices, lmk_bias, w_sizes, cu_seqlens, *,
+                             lmk_block: int = 0, cu_list=None):
+    """Drop-in for ``dsalt_triton_backward`` (``dsalt/kernels/dsalt_triton_bwd.py:219-323``):
+    ``(dq [T,H,D], dk [T,H_kv,D], dv [T,H_kv,D], d_bias [H,n_sets,k])``, all fp32.
+
+    ``out`` is the forward's output (its values in the input dtype, as the reference keeps
+    them) and ``lse`` its log-sum-exp (``dsalt_attention(..., return_lse=True)``);
+    ``grad_out`` is taken in the input dtype for bf16/fp16 inputs, as the reference's
+    ``do_f``. ``d_bias`` follows the caller's slot order of ``lmk_indices``."""
+    _cuda(q, k, v, out, grad_out, lse, lmk_indices, w_sizes, cu_seqlens)
+    T, H, D = q.shape
+    n_kv = k.shape[1]
+    dt = q.dtype
+    qc = q if (q.stride(2) == 1 and q.stride(1) == D) else q.contiguous()
+    kc = k.contiguous() if not (k.stride(2) == 1 and k.stride(1) == D) else k
+    vc = v.contiguous() if not (v.stride(2) == 1 and v.stride(1) == D) else v
+    if kc.stride(0) != vc.stride(0):
+        kc, vc = kc.contiguous(), vc.contiguous()
+    do = grad_out.to(dt if dt != torch.float32 else torch.float32).contiguous()
+    oc = out.contiguous()
+    cu_h = _host_cu(cu_seqlens, cu_list)
+    S = len(cu_h) - 1
+    lmk, bias = normalize_landmarks(lmk_indices, lmk_bias)
+    kl = int(lmk.shape[-1])
+    n_sets = int(lmk.shape[1])
+    dq = torch.empty(T, H, D, dtype=torch.float32, device=q.device)
+    dk = torch.empty(T, n_kv, D, dtype=torch.float32, device=q.device)
+    dv = torch.empty(T, n_kv, D, dtype=torch.float32, device=q.device)
+    db = torch.empty(H, n_sets, kl, dtype=torch.float32, device=q.device)
+    ws = _workspace(L.query("dsalt_attention_bwd_workspace_bytes", T, S), q.device)
+    L.call("dsalt_attention_bwd", _ptr(qc), _ptr(kc), _ptr(vc), _dt(qc), T, H, n_kv, D, qc.stride(0), kc.stride(0),
+           _ptr(oc), _dt(oc), _ptr(do), _dt(do), _ptr(lse.contiguous()), _ptr(w_sizes.to(torch.int32).contiguous()),
+           _ptr(lmk), _ptr(bias), kl, int(lmk_block), n_sets, _ptr(_cu_i32(cu_seqlens)), S, _ptr(dq), _ptr(dk),
+           _ptr(dv), _ptr(db), _ptr(ws), ws.numel(), _stream())
+    # back to the caller's slot order (normalize_landmarks sorted each set)
+    raw = lmk_indices.to(torch.int32)
+    key = torch.where(raw < 0, torch.full_like(raw, torch.iinfo(torch.int32).max), raw)
+    order = torch.sort(key, dim=-1, stable=True).indices
+    d_bias = torch.empty_like(db).scatter_(-1, order, db)
+    return dq, dk, dv, d_bias
+
+
+class DSALTAttentionFunction(torch.autograd.Function):
+    """Autograd of the sparse attention (``DSALTAttentionFunction``,
+    ``dsalt/kernels/dsalt_triton_attn.py:257-327``): the forward kernel with its
+    log-sum-exp, the backward kernel for ``q``, ``k``, ``v`` and the landmark bias."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, lmk_block, cu_list):
+        out_raw, lse = dsalt_attention(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, lmk_block=lmk_block,
+                                       out_dtype=q.dtype, cu_list=cu_list, return_lse=True)
+        ctx.save_for_backward(q, k, v, out_raw, lse, lmk_indices, lmk_bias if lmk_bias is not None else q.new_empty(0),
+                              w_sizes, cu_seqlens)
+        ctx.has_bias = lmk_bias is not None
+        ctx.lmk_block, ctx.cu_list = lmk_block, cu_list
+        return out_raw.float()
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k, v, out_raw, lse, lmk, bias, w, cu = ctx.saved_tensors
+        dq, dk, dv, db = dsalt_attention_backward(grad_out, q, k, v, out_raw, lse, lmk, bias if ctx.has_bias else None,
+                                                  w, cu, lmk_block=ctx.lmk_block, cu_list=ctx.cu_list)
+        d_bias = db.to(bias.dtype) if ctx.has_bias else None
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, d_bias, None, None, None, None
+
+
+def dsalt_attention_autograd(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, *, lmk_block: int = 0,
+                             cu_list=None):
+    """``dsalt_triton_attention`` with gradients (``dsalt_triton_attn.py:337-349``): fp32
+    output, differentiable in ``q``, ``k``, ``v`` and ``lmk_bias``."""
+    return DSALTAttentionFunction.apply(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, int(lmk_block), cu_list)
+
+
 # --------------------------------------------------------------------------- fused core
 def core_forward(x, gate_weight, gate_bias, n_min, n_max, alpha, q, k, v, k_lmk, cu_seqlens, *, mode="global",
                  block=512, norm_round=False, out_dtype=None, cu_list=None, return_aux=False, workspace=None,

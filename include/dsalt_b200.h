@@ -130,6 +130,30 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
                         size_t workspace_bytes, void* stream);
 
 /*
+ * Backward of the sparse attention forward above.
+ * Replaces dsalt_triton_backward / DSALTAttentionFunction.backward
+ *   (dsalt/kernels/dsalt_triton_bwd.py:219-323, dsalt_triton_attn.py:313-327), i.e.
+ *   _dsalt_bwd_preprocess (:18-49) and _dsalt_bwd_kernel (:52-216).
+ *
+ * q, k, v, w, lmk, lmk_bias, lmk_block, cu_seqlens as for the forward (lmk in the forward's
+ *   ascending format); n_sets = lmk's second extent. out [T, n_heads, head_dim] is the
+ *   forward's output in out_dtype and dout [T, n_heads, head_dim] its gradient in
+ *   dout_dtype (both contiguous); lse [T, n_heads] fp32 the forward's log-sum-exp (natural
+ *   log, -inf for rows with no key). Outputs (fp32, overwritten): dq [T, n_heads, head_dim],
+ *   dk / dv [T, n_kv, head_dim] (summed over the heads of each kv group), d_bias
+ *   [n_heads, n_sets, k_lmk] (nullable). head_dim 64 or 128; lmk_block a multiple of 64.
+ *   CUDA cores in fp32; dk, dv and d_bias accumulate with atomic adds, so their last bits
+ *   vary from run to run.
+ */
+size_t dsalt_attention_bwd_workspace_bytes(int64_t T, int n_seqs);
+int dsalt_attention_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
+                        int head_dim, int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype,
+                        const void* dout, int dout_dtype, const float* lse, const int32_t* w, const int32_t* lmk,
+                        const float* lmk_bias, int k_lmk, int lmk_block, int n_sets, const int32_t* cu_seqlens,
+                        int n_seqs, float* dq, float* dk, float* dv, float* d_bias, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/*
  * Sequence-sharded forms (no counterpart in the reference, which runs on one GPU): one
  * rank's share of a single sequence of seq_len positions split across ranks.
  *

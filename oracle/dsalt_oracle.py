@@ -574,3 +574,69 @@ def masked_sdpa_forward(q, k, v, x_signals_scores, w, cu_seqlens, k_lmk):
     o = torch.nn.functional.scaled_dot_product_attention(
         qt.transpose(0, 1)[None], kt.transpose(0, 1)[None], vt.transpose(0, 1)[None], attn_mask=add[None, None])
     return o[0].transpose(0, 1).numpy()
+
+
+# --------------------------------------------------------------------------- #
+# backward of the inference kernel -- dsalt/kernels/dsalt_triton_bwd.py:18-216
+# --------------------------------------------------------------------------- #
+def attention_backward(q, k, v, out, dout, lse, w, lmk, cu_seqlens, lmk_block=0, lmk_bias=None, scale=None):
+    """Gradients of :func:`attention_forward` in float64, with the reference backward's
+    recomputation: ``delta = Σ_d O·dO`` (``_dsalt_bwd_preprocess``, ``:18-49``), and for each
+    key of the row's set (window, then landmarks with the causal and de-duplicating rule)
+    ``p = exp(q·k·scale (+ bias) − lse)``, ``ds = p (dO·v − delta) scale``; ``dq += ds k``,
+    ``dk += ds q``, ``dv += p dO`` (``:110-212``), ``d_bias[h, set, slot] += p (dO·v − delta)``
+    (``:153-155``). Rows whose ``lse`` is ``-inf`` contribute nothing. ``k`` / ``v`` may have
+    fewer (grouped) heads than ``q``: head ``h`` uses kv head ``h // (H / H_kv)`` and the kv
+    gradients sum over the group. Returns ``(dq [T,H,D], dk, dv [T,H_kv,D], d_bias)``."""
+    q = np.asarray(q, dtype=F64)
+    k = np.asarray(k, dtype=F64)
+    v = np.asarray(v, dtype=F64)
+    out = np.asarray(out, dtype=F64)
+    dout = np.asarray(dout, dtype=F64)
+    lse = np.asarray(lse, dtype=F64)
+    T, H, D = q.shape
+    Hkv = k.shape[1]
+    rep = H // Hkv
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    scale = F64(F32(scale))
+    w = np.maximum(np.asarray(w, dtype=np.int64), 1)
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    d_bias = np.zeros(np.asarray(lmk).shape, dtype=F64)
+    delta = np.sum(out * dout, axis=-1)
+    S = len(cu_seqlens) - 1
+    set_base = 0
+    for s in range(S):
+        a, b = int(cu_seqlens[s]), int(cu_seqlens[s + 1])
+        L = b - a
+        nsets = 1 if lmk_block == 0 else max((L + lmk_block - 1) // lmk_block, 0)
+        for i in range(L):
+            t = a + i
+            lo = i - int(w[t]) + 1
+            j0 = max(lo, 0)
+            set_id = set_base if lmk_block == 0 else set_base + i // lmk_block
+            for h in range(H):
+                if not np.isfinite(lse[t, h]):
+                    continue
+                g = h // rep
+                rows = np.arange(a + j0, a + i + 1)
+                P = np.asarray(lmk)[h, set_id]
+                ok = (P >= 0) & (P < L) & (P <= i) & (P < lo)
+                slots = np.nonzero(ok)[0]
+                rows = np.concatenate([rows, a + P[slots].astype(np.int64)])
+                lg = k[rows, g] @ q[t, h] * scale
+                nw = i + 1 - j0
+                if lmk_bias is not None:
+                    lg[nw:] += np.asarray(lmk_bias, dtype=F64)[h, set_id][slots]
+                p = np.exp(lg - lse[t, h])
+                dp = v[rows, g] @ dout[t, h]
+                rec = p * (dp - delta[t, h])
+                ds = rec * scale
+                dq[t, h] += ds @ k[rows, g]
+                np.add.at(dk[:, g], rows, ds[:, None] * q[t, h][None, :])
+                np.add.at(dv[:, g], rows, p[:, None] * dout[t, h][None, :])
+                d_bias[h, set_id, slots] += rec[nw:]
+        set_base += nsets
+    return dq, dk, dv, d_bias
