@@ -350,8 +350,15 @@ def run_sharded(args, rank, world, local, dev):
     barrier(world)
     torch.cuda.synchronize()
     # one nvidia-smi, on rank 0, samples rank 0's GPU: an nvidia-smi that queries every GPU of
-    # the node stalled them (N = 2: 0.78 -> 6.1 ms per step), one per rank cost ~2 % at N = 2
+    # the node stalled them (N = 2: 0.78 -> 6.1 ms per step), one per rank cost ~2 % at N = 2.
+    # Host stalls (eight ranks and the sampler on one host) must not starve the GPUs inside
+    # the timed region: each stream is held by a device-side sleep while the host queues every
+    # timed step behind it, and the timer starts when the sleep ends. A one-element all-reduce
+    # queued first makes the sleeps start together on every GPU, whatever the hosts' timing.
+    align = torch.zeros(1, device=dev)
     with (ClockSampler(local) if rank == 0 else contextlib.nullcontext()) as clk:
+        torch.distributed.all_reduce(align)
+        torch.cuda._sleep(int(0.03 * 1.9e9))  # ~30 ms of GPU clocks, outside the timed region
         e0.record(stream)
         steps(args.steps)
         e1.record(stream)
@@ -360,8 +367,10 @@ def run_sharded(args, rank, world, local, dev):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     status = ops.device_status()
     # per-phase breakdown of one more (uncaptured) step: CUDA events on this rank's stream,
-    # max over ranks; the GPU first sleeps ~5 ms so that every launch is queued before it runs
+    # max over ranks; the GPUs first sleep ~5 ms together (after an aligning all-reduce) so that
+    # every launch is queued before it runs
     evs = []
+    torch.distributed.all_reduce(align)
     torch.cuda._sleep(10_000_000)
     core.forward(xs, gw, gb, alpha, qs, events=evs)
     torch.cuda.synchronize()
