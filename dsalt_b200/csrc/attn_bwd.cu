@@ -12,7 +12,9 @@
 // CUDA cores, fp32 throughout. One CTA per (64-query tile, head), 256 threads; the key axis is
 // walked in 32-key tiles: the window band of the tile, then the landmark slots of its set.
 // Per key tile the Q/dO tile (resident), the K/V tile and the P/dS tile sit in shared memory
-// with padded rows (stride HD + 1 floats: the 32 banks see distinct rows).
+// with padded rows (stride HD + 1 floats: the 32 banks see distinct rows); every thread
+// computes 2 x 4 (P, dS), 2 rows of dQ and 2 keys of dK / dV (register blocking: ~0.7
+// shared-memory operands per FMA instead of ~1.1).
 #include "common.cuh"
 
 namespace dsalt {
@@ -144,7 +146,7 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
   const int32_t* P = p.lmk + ((int64_t)h * n_sets + set) * p.k_lmk;
   const float* Bset = p.lmk_bias ? p.lmk_bias + ((int64_t)h * n_sets + set) * p.k_lmk : nullptr;
 
-  // this thread's share of dQ: row tid >> 2, dims (tid & 3) + 4 m
+  // this thread's share of dQ: rows (tid >> 3) + 32 u, dims (tid & 7) + 8 m at dq_acc[u * HD/8 + m]
   float dq_acc[HD / 4];
 #pragma unroll
   for (int m = 0; m < HD / 4; ++m) dq_acc[m] = 0.f;
@@ -180,82 +182,101 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
       sv[c * LD + d] = vv;
     }
     __syncthreads();
-    // P and dS: thread -> row tid >> 2, columns (tid & 3) + 4 j
+    // P and dS: thread -> rows rA, rA + 32 and keys c0 + 8 j (2 x 4 entries; per head-dim
+    // step 4 + 8 shared-memory operands for 16 FMAs)
     {
-      const int r = tid >> 2, c0 = tid & 3;
-      float sacc[BN / 4], dpacc[BN / 4];
+      const int rA = tid >> 3, c0 = tid & 7;
+      float sacc[2][4], dpacc[2][4];
 #pragma unroll
-      for (int j = 0; j < BN / 4; ++j) sacc[j] = dpacc[j] = 0.f;
-      const float* qr = sq + r * LD;
-      const float* dor = sdo + r * LD;
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sacc[u][j] = dpacc[u][j] = 0.f;
 #pragma unroll 4
       for (int d = 0; d < HD; ++d) {
-        const float a = qr[d], b = dor[d];
+        const float a0 = sq[rA * LD + d], a1 = sq[(rA + 32) * LD + d];
+        const float b0 = sdo[rA * LD + d], b1 = sdo[(rA + 32) * LD + d];
 #pragma unroll
-        for (int j = 0; j < BN / 4; ++j) {
-          const int c = c0 + 4 * j;
-          sacc[j] = fmaf(a, sk[c * LD + d], sacc[j]);
-          dpacc[j] = fmaf(b, sv[c * LD + d], dpacc[j]);
+        for (int j = 0; j < 4; ++j) {
+          const float kv = sk[(c0 + 8 * j) * LD + d], vv = sv[(c0 + 8 * j) * LD + d];
+          sacc[0][j] = fmaf(a0, kv, sacc[0][j]);
+          sacc[1][j] = fmaf(a1, kv, sacc[1][j]);
+          dpacc[0][j] = fmaf(b0, vv, dpacc[0][j]);
+          dpacc[1][j] = fmaf(b1, vv, dpacc[1][j]);
         }
       }
-      const int i = m0 + r;
-      const bool ok = row_ok[r];
-      const int lo = row_lo[r];
-      const float l = row_lse[r], dl = row_delta[r];
 #pragma unroll
-      for (int j = 0; j < BN / 4; ++j) {
-        const int c = c0 + 4 * j;
-        const int pos = key_pos[c];
-        bool valid = ok && pos >= 0;
-        float logit = sacc[j] * p.scale;
-        if (is_w) {
-          valid = valid && pos >= lo && pos <= i;
-        } else {
-          valid = valid && pos <= i && pos < lo;
-          if (valid && Bset) logit += Bset[key_slot[c]];
+      for (int u = 0; u < 2; ++u) {
+        const int r = rA + 32 * u;
+        const int i = m0 + r;
+        const bool ok = row_ok[r];
+        const int lo = row_lo[r];
+        const float l = row_lse[r], dl = row_delta[r];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = c0 + 8 * j;
+          const int pos = key_pos[c];
+          bool valid = ok && pos >= 0;
+          float logit = sacc[u][j] * p.scale;
+          if (is_w) {
+            valid = valid && pos >= lo && pos <= i;
+          } else {
+            valid = valid && pos <= i && pos < lo;
+            if (valid && Bset) logit += Bset[key_slot[c]];
+          }
+          const float pr = valid ? expf(logit - l) : 0.f;
+          sp[r * (BN + 1) + c] = pr;
+          sds[r * (BN + 1) + c] = pr * (dpacc[u][j] - dl);  // scaled below where dS is used
         }
-        const float pr = valid ? expf(logit - l) : 0.f;
-        const float rec = pr * (dpacc[j] - dl);
-        sp[r * (BN + 1) + c] = pr;
-        sds[r * (BN + 1) + c] = rec;  // scaled below where dS is used
       }
     }
     __syncthreads();
-    // dQ += dS · K (dS = rec · scale)
+    // dQ += dS · K (dS = rec · scale): thread -> rows rA, rA + 32 and dims d0 + 8 m
     {
-      const int r = tid >> 2, d0 = tid & 3;
-      const float* dsr = sds + r * (BN + 1);
+      const int rA = tid >> 3, d0 = tid & 7;
 #pragma unroll 4
       for (int c = 0; c < BN; ++c) {
-        const float ds = dsr[c] * p.scale;
+        const float ds0 = sds[rA * (BN + 1) + c] * p.scale, ds1 = sds[(rA + 32) * (BN + 1) + c] * p.scale;
 #pragma unroll
-        for (int m = 0; m < HD / 4; ++m) dq_acc[m] = fmaf(ds, sk[c * LD + d0 + 4 * m], dq_acc[m]);
-      }
-    }
-    // dK_tile = dSᵀ · Q, dV_tile = Pᵀ · dO: thread -> key tid >> 3, dims (tid & 7) + 8 m
-    {
-      const int c = tid >> 3, d0 = tid & 7;
-      constexpr int ND = HD / 8;
-      float dkacc[ND], dvacc[ND];
-#pragma unroll
-      for (int m = 0; m < ND; ++m) dkacc[m] = dvacc[m] = 0.f;
-#pragma unroll 4
-      for (int r = 0; r < BM; ++r) {
-        const float ds = sds[r * (BN + 1) + c] * p.scale, pr = sp[r * (BN + 1) + c];
-#pragma unroll
-        for (int m = 0; m < ND; ++m) {
-          dkacc[m] = fmaf(ds, sq[r * LD + d0 + 8 * m], dkacc[m]);
-          dvacc[m] = fmaf(pr, sdo[r * LD + d0 + 8 * m], dvacc[m]);
+        for (int m = 0; m < HD / 8; ++m) {
+          const float kv = sk[c * LD + d0 + 8 * m];
+          dq_acc[m] = fmaf(ds0, kv, dq_acc[m]);
+          dq_acc[HD / 8 + m] = fmaf(ds1, kv, dq_acc[HD / 8 + m]);
         }
       }
-      const int pos = key_pos[c];
-      if (pos >= 0) {
-        float* gk = p.dk + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
-        float* gv = p.dv + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
+    }
+    // dK_tile = dSᵀ · Q, dV_tile = Pᵀ · dO: thread -> keys kA, kA + 16 and dims d0 + 16 m
+    {
+      const int kA = tid >> 4, d0 = tid & 15;
+      constexpr int ND = HD / 16;
+      float dkacc[2][ND], dvacc[2][ND];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int m = 0; m < ND; ++m) dkacc[u][m] = dvacc[u][m] = 0.f;
+#pragma unroll 4
+      for (int r = 0; r < BM; ++r) {
+        const float ds0 = sds[r * (BN + 1) + kA] * p.scale, ds1 = sds[r * (BN + 1) + kA + 16] * p.scale;
+        const float p0 = sp[r * (BN + 1) + kA], p1 = sp[r * (BN + 1) + kA + 16];
 #pragma unroll
         for (int m = 0; m < ND; ++m) {
-          if (dkacc[m] != 0.f) atomicAdd(gk + d0 + 8 * m, dkacc[m]);
-          if (dvacc[m] != 0.f) atomicAdd(gv + d0 + 8 * m, dvacc[m]);
+          const float qv = sq[r * LD + d0 + 16 * m], dov = sdo[r * LD + d0 + 16 * m];
+          dkacc[0][m] = fmaf(ds0, qv, dkacc[0][m]);
+          dkacc[1][m] = fmaf(ds1, qv, dkacc[1][m]);
+          dvacc[0][m] = fmaf(p0, dov, dvacc[0][m]);
+          dvacc[1][m] = fmaf(p1, dov, dvacc[1][m]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int pos = key_pos[kA + 16 * u];
+        if (pos >= 0) {
+          float* gk = p.dk + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
+          float* gv = p.dv + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
+#pragma unroll
+          for (int m = 0; m < ND; ++m) {
+            if (dkacc[u][m] != 0.f) atomicAdd(gk + d0 + 16 * m, dkacc[u][m]);
+            if (dvacc[u][m] != 0.f) atomicAdd(gv + d0 + 16 * m, dvacc[u][m]);
+          }
         }
       }
     }
@@ -268,14 +289,15 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
     }
     __syncthreads();
   }
-  // dQ of this thread's row and dims
-  {
-    const int r = tid >> 2, d0 = tid & 3;
+  // dQ of this thread's rows and dims
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int r = (tid >> 3) + 32 * u, d0 = tid & 7;
     const int i = m0 + r;
     if (i < L) {
       float* g = p.dq + ((seq0 + i) * (int64_t)p.H + h) * HD;
 #pragma unroll
-      for (int m = 0; m < HD / 4; ++m) g[d0 + 4 * m] = dq_acc[m];
+      for (int m = 0; m < HD / 8; ++m) g[d0 + 8 * m] = dq_acc[u * (HD / 8) + m];
     }
   }
 }
