@@ -464,6 +464,48 @@ PREFILL = {
 }
 
 
+def run_backward(args):
+    """The attention backward (``dsalt_attention_bwd``, the reference's ``dsalt_triton_backward``)
+    on the core's inputs at ``--seq-len``: block-causal sets of 512 queries, k = 128, H = 16,
+    D = 64, bf16, one GPU. ``value`` counts query rows per second; ``useful_tflops`` counts the
+    five length-D products per (query, key of A(i)) pair, landmark pairs bounded by 512 rows
+    per valid slot."""
+    from dsalt_b200 import ops
+    dev = torch.device("cuda", 0)
+    T, H, D, k, B = CFG["L"], CFG["H"], CFG["D"], CFG["k"], CFG["block"]
+    x, gw, gb, alpha, q, kk, v = make_inputs(dev)
+    cu = [0, T]
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    _, w, lmk = ops.core_forward(x, gw, gb, CFG["n_min"], CFG["n_max"], alpha, q, kk, v, k, cu_t,
+                                 mode="block_causal", block=B, cu_list=cu, return_aux=True)
+    out, lse = ops.dsalt_attention(q, kk, v, lmk, None, w, cu_t, lmk_block=B, out_dtype=torch.bfloat16, cu_list=cu,
+                                   return_lse=True)
+    dout = torch.randn(out.shape, device=dev, generator=torch.Generator(device=dev).manual_seed(1)).to(out.dtype)
+
+    def step():
+        return ops.dsalt_attention_backward(dout, q, kk, v, out, lse, lmk, None, w, cu_t, lmk_block=B, cu_list=cu)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    i = torch.arange(T, device=dev)
+    pairs = int(torch.minimum(w.long().clamp(min=1), i + 1).sum()) + int((lmk >= 0).sum()) * B // H
+    print(json.dumps({"metric": "DSALT attention backward query rows/s", "value": T / (ms / 1e3), "unit": "rows/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                      "higher_is_better": True, "dtype": "bf16 inputs, fp32 arithmetic", "data": "synthetic",
+                      "config": {"workload": f"dsalt_attn_bwd_L{T}_H{H}_D{D}_k{k}_block{B}", "L": T},
+                      "useful_tflops": pairs * H * 10 * D / ms / 1e9, "clocks": clk.summary(),
+                      "device_status": ops.device_status()}), flush=True)
+
+
 def run_prefill(args):
     """Full-model prefill on one GPU: random-init bf16
     weights, uniform random token ids from a seed, every layer's attention on this
@@ -515,9 +557,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="core", choices=["core", *PREFILL],
-                    help="core: the DSALT attention core (the benchmark); prefill_cfg3 / prefill_cfg5: full-model "
-                         "prefill of BASELINE configs[2] / configs[4] on one GPU")
+    ap.add_argument("--workload", default="core", choices=["core", "backward", *PREFILL],
+                    help="core: the DSALT attention core (the benchmark); backward: the attention backward on the "
+                         "core's inputs; prefill_cfg3 / prefill_cfg5: full-model prefill of BASELINE configs[2] / "
+                         "configs[4] on one GPU")
     ap.add_argument("--seq-len", type=int, default=CFG["L"],
                     help="sequence length (131072 is the benchmark; shorter ones for profiler captures)")
     args = ap.parse_args()
@@ -526,6 +569,9 @@ def main():
         CFG["workload"] = CFG["workload"].replace("L131072", f"L{args.seq_len}")
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "backward":
+        args.warmup = max(args.warmup, 3)
+        return run_backward(args)
     if args.workload != "core":
         args.warmup = max(args.warmup, 3)
         return run_prefill(args)
