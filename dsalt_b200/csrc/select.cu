@@ -37,7 +37,6 @@ constexpr int SEL_THREADS = 512;
 constexpr int KEY_CAP = 8192;            // candidate keys cached in shared memory
 constexpr int BSEL_THREADS = 256;        // block-causal select: small CTAs, several per SM
 constexpr int BSEL_KEY_CAP = 1536;       // its key cache (the prefix-dominance filter keeps ~1K)
-constexpr int BSEL_REC_CAP = 4608;       // survivors whose chunk index is tabulated
 constexpr int MAX_K = 1024;
 
 // thresholds (in units of the sequence's std above its mean) of the dominance grid:
@@ -798,22 +797,68 @@ __global__ void __launch_bounds__(512) survivor_all_kernel(
   if (threadIdx.x < gpb) surv_cnt[(int64_t)c * n_kv + g0 + threadIdx.x] = cnt[threadIdx.x];
 }
 
+// Packs every kv group's survivor records in chunk order, so that a block's candidates (the
+// survivors of its sequence's earlier chunks) form one contiguous run: poff[c][g] = records of
+// group g in chunks [0, c) (all sequences in turn; entry n_chunks holds the total), then a
+// copy of each (chunk, group) list to its offset. n_chunks < 0: every chunk of the tables.
+__global__ void __launch_bounds__(1024) survivor_offsets_kernel(const int32_t* __restrict__ cnt, int n_kv,
+                                                                 const int32_t* __restrict__ base, int n_seqs,
+                                                                 int n_chunks, int32_t* __restrict__ poff) {
+  __shared__ int32_t wsum[32];
+  const int g = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int nc = n_chunks >= 0 ? n_chunks : base[n_seqs];
+  int carry = 0;
+  for (int c0 = 0; c0 < nc; c0 += blockDim.x) {
+    const int c = c0 + threadIdx.x;
+    const int v = c < nc ? cnt[(int64_t)c * n_kv + g] : 0;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[wid] = x;
+    __syncthreads();
+    int before = carry, tot = 0;
+    for (int q = 0; q < nw; ++q) {
+      if (q < wid) before += wsum[q];
+      tot += wsum[q];
+    }
+    if (c < nc) poff[(int64_t)c * n_kv + g] = before + x - v;
+    carry += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) poff[(int64_t)nc * n_kv + g] = carry;
+}
+
+__global__ void pack_survivors_kernel(const int32_t* __restrict__ cnt, const int4* __restrict__ recs,
+                                      const int32_t* __restrict__ poff, int n_kv, int C,
+                                      const int32_t* __restrict__ base, int n_seqs, int n_chunks,
+                                      int4* __restrict__ packed, int64_t rec_stride) {
+  const int c = blockIdx.x, g = blockIdx.y;
+  const int nc = n_chunks >= 0 ? n_chunks : base[n_seqs];
+  if (c >= nc) return;
+  const int64_t cg = (int64_t)c * n_kv + g;
+  const int n = cnt[cg];
+  const int4* src = recs + cg * C;
+  int4* dst = packed + (int64_t)g * rec_stride + poff[cg];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+
+
 // per (block set, head): exact scores of the surviving candidates of earlier chunks
 __global__ void __launch_bounds__(BSEL_THREADS, 6) block_select_kernel(
     const float* __restrict__ xn, const float* __restrict__ vn, const int32_t* __restrict__ w,
     const float* __restrict__ alpha, const int32_t* __restrict__ cu, int n_seqs, const int32_t* __restrict__ base,
     int C, int n_heads, int n_kv, int k, const double2* __restrict__ stats, const int32_t* __restrict__ D,
-    const int32_t* __restrict__ surv_cnt, const int4* __restrict__ surv_rec, int32_t* __restrict__ lmk_out, int set_lo,
-    int n_out) {
+    const int32_t* __restrict__ poff, const int4* __restrict__ packed, int64_t rec_stride, int32_t* __restrict__ lmk_out,
+    int set_lo, int n_out) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint64_t* keys = reinterpret_cast<uint64_t*>(smem_raw);
   __shared__ TopkSmem sm;
   __shared__ int32_t sel[MAX_K];
-  __shared__ int32_t offs[1025];
-  __shared__ int32_t wsum[32];
   __shared__ int32_t dsm[NCELL];
   __shared__ int32_t ncand;
-  __shared__ uint16_t chunk_of[BSEL_REC_CAP];  // survivor index -> chunk (when they fit)
   // sets set_lo + blockIdx.x; output [H, n_out, k] (n_out = all sets, or the range's)
   const int c = set_lo + blockIdx.x, h = blockIdx.y;
   const int total = base[n_seqs];
@@ -831,7 +876,7 @@ __global__ void __launch_bounds__(BSEL_THREADS, 6) block_select_kernel(
   const double2 stx = stats[(int64_t)c * nsig + 0];
   const double2 stv = stats[(int64_t)c * nsig + 1 + g];
   const float a = alpha[h];
-  const bool pruned = (a >= 0.0f && a <= 1.0f) && b <= 1024;
+  const bool pruned = a >= 0.0f && a <= 1.0f;
   const double rx = __drcp_rn(stx.y), rv = __drcp_rn(stv.y);
   auto score_key = [&](int p) -> uint64_t {
     const int64_t t = start + p;
@@ -852,33 +897,14 @@ __global__ void __launch_bounds__(BSEL_THREADS, 6) block_select_kernel(
     }
     return;
   }
-  // offsets of the survivor lists of chunks 0..b-1 of this sequence (b <= 1024)
+  // the survivor records of chunks c0 .. c0 + b - 1 of this sequence, packed per kv group
+  // (pack_survivors_kernel): one contiguous run of NS records
   const int c0 = base[s];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  int carry = 0;
-  for (int j0 = 0; j0 < b; j0 += blockDim.x) {
-    const int j = j0 + threadIdx.x;
-    const int v = j < b ? surv_cnt[(int64_t)(c0 + j) * n_kv + g] : 0;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) wsum[wid] = x;
-    __syncthreads();
-    int before = carry;
-    for (int q = 0; q < wid; ++q) before += wsum[q];
-    if (j < b) offs[j] = before + x - v;
-    int tot = 0;
-    for (int q = 0; q < (int)(blockDim.x >> 5); ++q) tot += wsum[q];
-    carry += tot;
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    offs[b] = carry;
-    ncand = 0;
-  }
+  const int lane = threadIdx.x & 31;
+  const int p_lo = poff[(int64_t)c0 * n_kv + g];
+  const int NS = poff[(int64_t)(c0 + b) * n_kv + g] - p_lo;
+  const int4* R = packed + (int64_t)g * rec_stride + p_lo;
+  if (threadIdx.x == 0) ncand = 0;
   // dominators of every grid cell among all uncovered tokens of the block's prefix
   const int32_t* Dc = D + ((int64_t)c * n_kv + g) * NCELL;
   for (int i = threadIdx.x; i < NCELL; i += blockDim.x) dsm[i] = Dc[i];
@@ -893,28 +919,7 @@ __global__ void __launch_bounds__(BSEL_THREADS, 6) block_select_kernel(
     const float sc = __fadd_rn(__fmul_rn(a, zv), __fmul_rn(a1, zx));
     return make_key(sc, r.x);
   };
-  // survivor i of the prefix lies in chunk j with offs[j] <= i < offs[j+1]
-  const int NS = offs[b];
-  const bool tab = NS <= BSEL_REC_CAP;
-  if (tab) {
-    for (int j = wid; j < b; j += (int)(blockDim.x >> 5))
-      for (int i = offs[j] + lane; i < offs[j + 1]; i += 32) chunk_of[i] = (uint16_t)j;
-    __syncthreads();
-  }
-  auto rec_of = [&](int i) -> const int4* {
-    int lo = 0;
-    if (tab) {
-      lo = chunk_of[i];
-    } else {
-      int hi = b;
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (offs[mid] <= i) lo = mid;
-        else hi = mid;
-      }
-    }
-    return surv_rec + ((int64_t)(c0 + lo) * n_kv + g) * C + (i - offs[lo]);
-  };
+  auto rec_of = [&](int i) -> const int4* { return R + i; };
   constexpr int U = 4;  // records per thread in flight
   for (int i0 = threadIdx.x; i0 - (int)threadIdx.x < NS; i0 += U * blockDim.x) {
     int4 r[U];
@@ -956,7 +961,7 @@ static inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 struct SelectLayout {
   size_t base_off, part_off, gstats_off, gbase_off, cand_off, stats_off, edges_off, G_off, seg_off, cnt_off, pos_off,
-      total;
+      poff_off, pack_off, total;
   int max_chunks, max_gchunks, nsig, max_segs;
 };
 
@@ -992,9 +997,27 @@ static SelectLayout select_layout(int mode, int64_t T, int n_seqs, int n_heads, 
     off = align256(off + sizeof(int32_t) * (size_t)L.max_chunks * n_kv);
     L.pos_off = off;
     off = align256(off + sizeof(int4) * (size_t)L.max_chunks * n_kv * C);
+    L.poff_off = off;  // per (chunk, group): first packed survivor record (+ one end entry)
+    off = align256(off + sizeof(int32_t) * (size_t)(L.max_chunks + 1) * n_kv);
+    L.pack_off = off;  // per group: the survivor records of every chunk, in chunk order
+    off = align256(off + sizeof(int4) * (size_t)L.max_chunks * n_kv * C);
   }
   L.total = off;
   return L;
+}
+
+static int launch_pack_survivors(const SelectLayout& L, char* ws, int n_kv, int C, const int32_t* cbase, int n_seqs,
+                                 int n_chunks, cudaStream_t stream) {
+  const int32_t* cnt = reinterpret_cast<const int32_t*>(ws + L.cnt_off);
+  const int4* recs = reinterpret_cast<const int4*>(ws + L.pos_off);
+  int32_t* poff = reinterpret_cast<int32_t*>(ws + L.poff_off);
+  int4* packed = reinterpret_cast<int4*>(ws + L.pack_off);
+  survivor_offsets_kernel<<<n_kv, 1024, 0, stream>>>(cnt, n_kv, cbase, n_seqs, n_chunks, poff);
+  const int grid_c = n_chunks >= 0 ? n_chunks : L.max_chunks;
+  if (grid_c > 0)
+    pack_survivors_kernel<<<dim3(grid_c, n_kv), 64, 0, stream>>>(cnt, recs, poff, n_kv, C, cbase, n_seqs, n_chunks,
+                                                                  packed, (int64_t)L.max_chunks * C);
+  return check_cuda(cudaGetLastError(), "survivor packing launch");
 }
 
 size_t select_workspace_bytes(int mode, int64_t T, int n_seqs, int max_seqlen, int n_heads, int n_kv, int k,
@@ -1097,11 +1120,14 @@ int launch_select(int mode, const float* xnorm, const float* vnorm, const int32_
       survivor_kernel<<<dim3(L.max_chunks, n_kv), 256, 0, stream>>>(xnorm, vnorm, w, n_kv, cu, n_seqs, cbase, C,
                                                                     edges, G, k, cnt, recs);
     }
+    int rc2 = launch_pack_survivors(L, ws, n_kv, C, cbase, n_seqs, -1, stream);
+    if (rc2) return rc2;
     const size_t sm3 = sizeof(uint64_t) * BSEL_KEY_CAP;
     const bool range = set_hi >= 0;
     block_select_kernel<<<dim3(range ? set_hi - set_lo : L.max_chunks, n_heads), BSEL_THREADS, sm3, stream>>>(
-        xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, G, cnt, recs, lmk_out,
-        range ? set_lo : 0, range ? set_hi - set_lo : 0);
+        xnorm, vnorm, w, alpha, cu, n_seqs, cbase, C, n_heads, n_kv, k, stats, G,
+        reinterpret_cast<const int32_t*>(ws + L.poff_off), reinterpret_cast<const int4*>(ws + L.pack_off),
+        (int64_t)L.max_chunks * C, lmk_out, range ? set_lo : 0, range ? set_hi - set_lo : 0);
   }
   return check_cuda(cudaGetLastError(), "select launch");
 }
@@ -1308,9 +1334,12 @@ int launch_select_shard(int phase, const float* xnorm, const float* vnorm, const
     if (c_lo > 0)
       gather_survivors_kernel<<<dim3(c_lo, n_kv), 64, 0, stream>>>(cnt, recs, peers, L.cnt_off, L.pos_off, n_kv, C,
                                                                    cpr);
+    if ((rc = launch_pack_survivors(L, ws, n_kv, C, cbase, 1, c_hi, stream))) return rc;
     const size_t sm3 = sizeof(uint64_t) * BSEL_KEY_CAP;
     block_select_kernel<<<dim3(cpr, n_heads), BSEL_THREADS, sm3, stream>>>(
-        xnorm, vnorm, w, alpha, cu, 1, cbase, C, n_heads, n_kv, k, stats, G, cnt, recs, lmk_out, c_lo, cpr);
+        xnorm, vnorm, w, alpha, cu, 1, cbase, C, n_heads, n_kv, k, stats, G,
+        reinterpret_cast<const int32_t*>(ws + L.poff_off), reinterpret_cast<const int4*>(ws + L.pack_off),
+        (int64_t)L.max_chunks * C, lmk_out, c_lo, cpr);
   }
   return check_cuda(cudaGetLastError(), "select shard launch");
 }
