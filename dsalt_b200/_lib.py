@@ -24,6 +24,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _I64 = ctypes.c_int64
 _SZ = ctypes.c_size_t
+_F = ctypes.c_float
 
 # name -> (restype, argtypes); the declarations of include/dsalt_b200.h
 SIGNATURES = {
@@ -41,6 +42,10 @@ SIGNATURES = {
     "dsalt_attention_bwd_workspace_bytes": (_SZ, [_I64, _I]),
     "dsalt_attention_bwd": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _I, _P, _I, _P, _P, _P, _P, _I, _I,
                                  _I, _P, _I, _P, _P, _P, _P, _P, _SZ, _P]),
+    "dsalt_train_attention_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P, _I, _P, _I, _F, _F,
+                                       _P, _I, _P, _P]),
+    "dsalt_train_attention_bwd": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _I, _P, _I, _P, _P, _P, _P,
+                                       _I, _P, _I, _F, _F, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "dsalt_attention_fwd_noalloc": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P, _I, _I, _P, _I,
                                          _I, _P, _I, _P, _P]),
     "dsalt_select_block_range_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I]),

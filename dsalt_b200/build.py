@@ -18,7 +18,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(OUT_DIR, "libdsalt_b200.so")
-SOURCES = ["capi.cu", "signals.cu", "select.cu", "attn_simt.cu", "attn_tc.cu", "attn_bwd.cu", "peer.cu"]
+SOURCES = ["capi.cu", "signals.cu", "select.cu", "attn_simt.cu", "attn_tc.cu", "attn_bwd.cu", "attn_train.cu", "peer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

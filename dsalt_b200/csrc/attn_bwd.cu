@@ -33,7 +33,7 @@ struct Smem {
   static constexpr int Q_OFF = 0, DO_OFF = BM * LD, K_OFF = 2 * BM * LD, V_OFF = K_OFF + BN * LD;
   static constexpr int P_OFF = V_OFF + BN * LD, DS_OFF = P_OFF + BM * (BN + 1);
   static constexpr int FLOATS = DS_OFF + BM * (BN + 1);
-  static constexpr size_t BYTES = (size_t)FLOATS * 4 + BM * 16 + BN * 8;  // + per-row and per-key ints
+  static constexpr size_t BYTES = (size_t)FLOATS * 4 + BM * 20 + BN * 8;  // + per-row and per-key words
 };
 
 struct Params {
@@ -61,9 +61,14 @@ struct Params {
   float* dk;      // [T, Hkv, HD]
   float* dv;      // [T, Hkv, HD]
   float* d_bias;  // [H, n_sets, k] or null
+  // training mode (soft selectors): continuous widths w̃ [T], soft edge τ and core margin,
+  // gradient of w̃ summed over heads [T]; lmk_bias / d_bias are the landmark log-weights
+  const float* w_cont;
+  float tau, win_edge;
+  float* d_w;
 };
 
-template <int HD>
+template <int HD, bool TRAIN>
 __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
   using SM = Smem<HD>;
   constexpr int LD = SM::LD;
@@ -78,7 +83,8 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
   int* row_ok = row_lo + BM;                                // per row: valid and finite lse
   float* row_lse = reinterpret_cast<float*>(row_ok + BM);
   float* row_delta = row_lse + BM;
-  int* key_pos = reinterpret_cast<int*>(row_delta + BM);    // per key of the tile: position or -1
+  float* row_wc = row_delta + BM;                           // per row: continuous width (training mode)
+  int* key_pos = reinterpret_cast<int*>(row_wc + BM);       // per key of the tile: position or -1
   int* key_slot = key_pos + BN;                             // landmark slot (or -1 for window keys)
 
   const int tile = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
@@ -122,16 +128,22 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     if (part == 0) {
-      float l = -INFINITY;
+      float l = -INFINITY, wc = 0.f;
       int lo = 0x3fffffff;
       if (i < L) {
         const int64_t t = seq0 + i;
         l = p.lse[t * p.H + h];
-        lo = i - max(p.w[t], 1) + 1;
+        if constexpr (TRAIN) {
+          wc = p.w_cont[t];  // band d = i - j in [0, w̃]: j from i - floor(w̃)
+          lo = wc >= 0.f ? i - (int)floorf(wc) : i + 1;
+        } else {
+          lo = i - max(p.w[t], 1) + 1;
+        }
       }
       row_delta[r] = acc;
       row_lse[r] = l;
       row_lo[r] = lo;
+      row_wc[r] = wc;
       row_ok[r] = (i < L) && (l > -INFINITY);
     }
   }
@@ -148,6 +160,7 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
 
   // this thread's share of dQ: rows (tid >> 3) + 32 u, dims (tid & 7) + 8 m at dq_acc[u * HD/8 + m]
   float dq_acc[HD / 4];
+  float dw_acc[2] = {0.f, 0.f};  // training mode: this thread's part of dL/dw̃ of its two rows
 #pragma unroll
   for (int m = 0; m < HD / 4; ++m) dq_acc[m] = 0.f;
 
@@ -210,22 +223,36 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
         const int i = m0 + r;
         const bool ok = row_ok[r];
         const int lo = row_lo[r];
-        const float l = row_lse[r], dl = row_delta[r];
+        const float l = row_lse[r], dl = row_delta[r], wc = row_wc[r];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = c0 + 8 * j;
           const int pos = key_pos[c];
           bool valid = ok && pos >= 0;
           float logit = sacc[u][j] * p.scale;
+          float dbdw = 0.f;  // training mode: d(edge bias)/dw̃ of this window key
           if (is_w) {
-            valid = valid && pos >= lo && pos <= i;
+            if constexpr (TRAIN) {
+              const float d = (float)(i - pos);
+              valid = valid && pos <= i && d <= wc;
+              if (valid && !(d <= wc - p.win_edge)) {
+                const float z = (wc - d) / p.tau;
+                logit += -logf(1.0f + expf(-z));          // log σ(z)
+                dbdw = (1.0f - 1.0f / (1.0f + expf(-z))) / p.tau;
+              }
+            } else {
+              valid = valid && pos >= lo && pos <= i;
+            }
           } else {
-            valid = valid && pos <= i && pos < lo;
+            if constexpr (TRAIN) valid = valid && pos <= i && (float)pos < (float)i - wc;
+            else valid = valid && pos <= i && pos < lo;
             if (valid && Bset) logit += Bset[key_slot[c]];
           }
           const float pr = valid ? expf(logit - l) : 0.f;
+          const float rec = pr * (dpacc[u][j] - dl);
           sp[r * (BN + 1) + c] = pr;
-          sds[r * (BN + 1) + c] = pr * (dpacc[u][j] - dl);  // scaled below where dS is used
+          sds[r * (BN + 1) + c] = rec;  // scaled below where dS is used
+          if constexpr (TRAIN) dw_acc[u] = fmaf(rec, dbdw, dw_acc[u]);
         }
       }
     }
@@ -289,6 +316,18 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
     }
     __syncthreads();
   }
+  if constexpr (TRAIN) {
+    // dL/dw̃ per row: the 8 threads of a row pair hold parts of it (lanes 8k .. 8k+7)
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float v = dw_acc[u];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      const int r = (tid >> 3) + 32 * u;
+      if ((tid & 7) == 0 && m0 + r < L && v != 0.f) atomicAdd(p.d_w + seq0 + m0 + r, v);
+    }
+  }
   // dQ of this thread's rows and dims
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
@@ -311,8 +350,12 @@ int launch_attn_bwd(const void* q, const void* k, const void* v, int dtype, int6
                     int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype, const void* dout,
                     int dout_dtype, const float* lse, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                     int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, float* dq, float* dk, float* dv,
-                    float* d_bias, void* workspace, size_t ws_bytes, cudaStream_t stream) {
+                    float* d_bias, void* workspace, size_t ws_bytes, cudaStream_t stream, const float* w_cont,
+                    float tau, float win_edge, float* d_w) {
   using namespace bwd;
+  const bool train = w_cont != nullptr;  // training mode: soft selectors (one set per sequence)
+  if (train && (lmk_block != 0 || !d_w || (k_lmk > 0 && !lmk_bias)))
+    return fail(DSALT_ERR_INVALID, "training attention backward: one set per sequence, log-weights and d_w needed");
   if (HD != 64 && HD != 128) return fail(DSALT_ERR_UNSUPPORTED, "attention backward: head_dim %d (64, 128)", HD);
   if (H < 1 || Hkv < 1 || H % Hkv) return fail(DSALT_ERR_INVALID, "attention backward: heads %d / kv heads %d", H, Hkv);
   if (lmk_block > 0 && lmk_block % BM)
@@ -354,8 +397,13 @@ int launch_attn_bwd(const void* q, const void* k, const void* v, int dtype, int6
   p.dk = dk;
   p.dv = dv;
   p.d_bias = d_bias;
+  p.w_cont = w_cont;
+  p.tau = tau;
+  p.win_edge = win_edge;
+  p.d_w = d_w;
   const int64_t max_tiles = T / BM + n_seqs;
-  auto kern = HD == 64 ? attn_bwd_kernel<64> : attn_bwd_kernel<128>;
+  auto kern = train ? (HD == 64 ? attn_bwd_kernel<64, true> : attn_bwd_kernel<128, true>)
+                    : (HD == 64 ? attn_bwd_kernel<64, false> : attn_bwd_kernel<128, false>);
   const size_t smem = HD == 64 ? Smem<64>::BYTES : Smem<128>::BYTES;
   if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "attention backward smem attr")))

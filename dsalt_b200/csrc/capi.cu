@@ -46,7 +46,12 @@ int launch_attn_bwd(const void* q, const void* k, const void* v, int dtype, int6
                     int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype, const void* dout,
                     int dout_dtype, const float* lse, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                     int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, float* dq, float* dk, float* dv,
-                    float* d_bias, void* workspace, size_t ws_bytes, cudaStream_t stream);
+                    float* d_bias, void* workspace, size_t ws_bytes, cudaStream_t stream,
+                    const float* w_cont = nullptr, float tau = 1.f, float win_edge = 0.f, float* d_w = nullptr);
+int launch_train_fwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int D,
+                     int64_t q_stride, int64_t kv_stride, const float* w_cont, const int32_t* lmk, const float* logw,
+                     int k_lmk, const int32_t* cu, int n_seqs, float tau, float win_edge, void* out, int out_dtype,
+                     float* lse, cudaStream_t stream);
 int launch_peer_barrier(int* own_flag, const int* const* flags, int n_ranks, int rank, int epoch, int* err,
                         cudaStream_t stream);
 int launch_peer_allgather(void* dst, const void* const* src, int n_ranks, int rank, int64_t bytes_per_rank,
@@ -217,6 +222,56 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
   return launch_attn_tc(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w, lmk, lmk_bias, k_lmk,
                         lmk_block, cu_seqlens, n_seqs, set_base, tile_base, plan, attention_max_tiles(T, n_seqs), out,
                         out_dtype, lse, device_status_ptr(), s);
+}
+
+int dsalt_train_attention_fwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads,
+                              int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, const float* w_cont,
+                              const int32_t* lmk, const float* lmk_logw, int k_lmk, const int32_t* cu_seqlens,
+                              int n_seqs, float tau_win, float win_edge, void* out, int out_dtype, float* lse,
+                              void* stream) {
+  if (T < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || n_seqs < 1 || k_lmk < 0 || !(tau_win > 0.f))
+    return fail(DSALT_ERR_INVALID, "training attention: bad sizes");
+  if (!valid_dtype(dtype) || !valid_dtype(out_dtype)) return fail(DSALT_ERR_INVALID, "training attention: dtype");
+  if (q_stride < (int64_t)n_heads * head_dim || kv_stride < (int64_t)n_kv * head_dim)
+    return fail(DSALT_ERR_INVALID, "training attention: token stride smaller than heads x head_dim");
+  if (T == 0) return DSALT_OK;
+  if (!q || !k || !v || !w_cont || !cu_seqlens || !out || (k_lmk > 0 && (!lmk || !lmk_logw)))
+    return fail(DSALT_ERR_INVALID, "training attention: null pointer");
+  return launch_train_fwd(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w_cont, lmk, lmk_logw,
+                          k_lmk, cu_seqlens, n_seqs, tau_win, win_edge, out, out_dtype, lse,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dsalt_train_attention_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
+                              int head_dim, int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype,
+                              const void* dout, int dout_dtype, const float* lse, const float* w_cont,
+                              const int32_t* lmk, const float* lmk_logw, int k_lmk, const int32_t* cu_seqlens,
+                              int n_seqs, float tau_win, float win_edge, float* dq, float* dk, float* dv,
+                              float* d_logw, float* d_w, void* workspace, size_t workspace_bytes, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (T < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || head_dim < 1 || n_seqs < 1 || k_lmk < 0 ||
+      !(tau_win > 0.f))
+    return fail(DSALT_ERR_INVALID, "training attention backward: bad sizes");
+  if (!valid_dtype(dtype) || !valid_dtype(out_dtype) || !valid_dtype(dout_dtype))
+    return fail(DSALT_ERR_INVALID, "training attention backward: dtype");
+  if (q_stride < (int64_t)n_heads * head_dim || kv_stride < (int64_t)n_kv * head_dim)
+    return fail(DSALT_ERR_INVALID, "training attention backward: token stride smaller than heads x head_dim");
+  if (T == 0) return DSALT_OK;
+  if (!q || !k || !v || !out || !dout || !lse || !w_cont || !cu_seqlens || !dq || !dk || !dv || !d_w ||
+      (k_lmk > 0 && (!lmk || !lmk_logw || !d_logw)) || !workspace)
+    return fail(DSALT_ERR_INVALID, "training attention backward: null pointer");
+  if (T > 0x7fffff00LL) return fail(DSALT_ERR_UNSUPPORTED, "training attention backward: T too large");
+  int rc;
+  if ((rc = check_cuda(cudaMemsetAsync(dk, 0, sizeof(float) * (size_t)T * n_kv * head_dim, s), "clear dk")) ||
+      (rc = check_cuda(cudaMemsetAsync(dv, 0, sizeof(float) * (size_t)T * n_kv * head_dim, s), "clear dv")) ||
+      (rc = check_cuda(cudaMemsetAsync(d_w, 0, sizeof(float) * (size_t)T, s), "clear d_w")))
+    return rc;
+  if (k_lmk > 0 && (rc = check_cuda(cudaMemsetAsync(d_logw, 0, sizeof(float) * (size_t)n_heads * n_seqs * k_lmk, s),
+                                    "clear d_logw")))
+    return rc;
+  return launch_attn_bwd(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, out, out_dtype, dout,
+                         dout_dtype, lse, nullptr, lmk, lmk_logw, k_lmk, 0, cu_seqlens, n_seqs, dq, dk, dv, d_logw,
+                         workspace, workspace_bytes, s, w_cont, tau_win, win_edge, d_w);
 }
 
 size_t dsalt_attention_bwd_workspace_bytes(int64_t T, int n_seqs) {

@@ -314,6 +314,89 @@ def dsalt_attention_autograd(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens
     return DSALTAttentionFunction.apply(q, k, v, lmk_indices, lmk_bias, w_sizes, cu_seqlens, int(lmk_block), cu_list)
 
 
+def train_attention_forward(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win: float, win_edge: float, *,
+                            out_dtype=None, cu_list=None):
+    """Forward of the soft-selector training attention (``_train_fwd_kernel``,
+    ``dsalt/kernels/dsalt_triton_train.py:74-217``): ``(out [T,H,D], lse [T,H])``. ``w_cont [T]``
+    continuous widths, ``lmk_pos [H, S, k]`` one landmark set per sequence (any order, ``-1``
+    = none), ``lmk_logw [H, S, k]`` their log-weights. ``out`` is in ``out_dtype`` (default:
+    the input dtype)."""
+    _cuda(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens)
+    T, H, D = q.shape
+    n_kv = k.shape[1]
+    qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+    cu_h = _host_cu(cu_seqlens, cu_list)
+    S = len(cu_h) - 1
+    kl = int(lmk_pos.shape[-1])
+    out = torch.empty(T, H, D, dtype=out_dtype or q.dtype, device=q.device)
+    lse = torch.empty(T, H, dtype=torch.float32, device=q.device)
+    L.call("dsalt_train_attention_fwd", _ptr(qc), _ptr(kc), _ptr(vc), _dt(qc), T, H, n_kv, D, qc.stride(0),
+           kc.stride(0), _ptr(w_cont.float().contiguous()), _ptr(lmk_pos.to(torch.int32).contiguous()),
+           _ptr(lmk_logw.float().contiguous()), kl, _ptr(_cu_i32(cu_seqlens)), S, float(tau_win), float(win_edge),
+           _ptr(out), _dt(out), _ptr(lse), _stream())
+    return out, lse
+
+
+def train_attention_backward(grad_out, q, k, v, out, lse, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win: float,
+                             win_edge: float, *, cu_list=None):
+    """Backward of :func:`train_attention_forward` (``_train_bwd_*``,
+    ``dsalt_triton_train.py:220-490``): ``(dq, dk [T,H_kv,D], dv, d_logw [H,S,k], d_w [T])``,
+    fp32; ``d_w`` is the gradient of the continuous widths summed over heads."""
+    _cuda(q, k, v, out, grad_out, lse, lmk_pos, lmk_logw, w_cont, cu_seqlens)
+    T, H, D = q.shape
+    n_kv = k.shape[1]
+    dt = q.dtype
+    qc, kc, vc, oc = q.contiguous(), k.contiguous(), v.contiguous(), out.contiguous()
+    do = grad_out.to(dt).contiguous()
+    cu_h = _host_cu(cu_seqlens, cu_list)
+    S = len(cu_h) - 1
+    kl = int(lmk_pos.shape[-1])
+    dq = torch.empty(T, H, D, dtype=torch.float32, device=q.device)
+    dk = torch.empty(T, n_kv, D, dtype=torch.float32, device=q.device)
+    dv = torch.empty(T, n_kv, D, dtype=torch.float32, device=q.device)
+    dlw = torch.empty(H, S, kl, dtype=torch.float32, device=q.device)
+    dw = torch.empty(T, dtype=torch.float32, device=q.device)
+    ws = _workspace(L.query("dsalt_attention_bwd_workspace_bytes", T, S), q.device)
+    L.call("dsalt_train_attention_bwd", _ptr(qc), _ptr(kc), _ptr(vc), _dt(qc), T, H, n_kv, D, qc.stride(0),
+           kc.stride(0), _ptr(oc), _dt(oc), _ptr(do), _dt(do), _ptr(lse.contiguous()),
+           _ptr(w_cont.float().contiguous()), _ptr(lmk_pos.to(torch.int32).contiguous()),
+           _ptr(lmk_logw.float().contiguous()), kl, _ptr(_cu_i32(cu_seqlens)), S, float(tau_win), float(win_edge),
+           _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dlw), _ptr(dw), _ptr(ws), ws.numel(), _stream())
+    return dq, dk, dv, dlw, dw
+
+
+class DSALTTrainFunction(torch.autograd.Function):
+    """``DSALTTrainFunction`` (``dsalt_triton_train.py:583-762``): fp32 output,
+    gradients for ``q``, ``k``, ``v``, the landmark log-weights (to alpha) and the continuous
+    widths (to ``win_gate``)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge, n_max, cu_list=None):
+        del n_max  # the reference's tile bound; the band here comes from w_cont itself
+        out, lse = train_attention_forward(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge,
+                                           cu_list=cu_list)
+        ctx.save_for_backward(q, k, v, out, lse, lmk_pos, lmk_logw, w_cont, cu_seqlens)
+        ctx.tau_win, ctx.win_edge, ctx.cu_list = float(tau_win), float(win_edge), cu_list
+        return out.float()
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        q, k, v, out, lse, lmk_pos, lmk_logw, w_cont, cu = ctx.saved_tensors
+        dq, dk, dv, dlw, dw = train_attention_backward(grad_out, q, k, v, out, lse, lmk_pos, lmk_logw, w_cont, cu,
+                                                       ctx.tau_win, ctx.win_edge, cu_list=ctx.cu_list)
+        od = q.dtype
+        return (dq.to(od), dk.to(k.dtype), dv.to(v.dtype), None, dlw.to(lmk_logw.dtype), dw.to(w_cont.dtype),
+                None, None, None, None, None)
+
+
+def dsalt_train_attention(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win=1.0, win_edge=4.0, n_max=256,
+                          cu_list=None):
+    """Drop-in for ``dsalt_triton_train_attention`` (``dsalt_triton_train.py:771-782``): differentiable
+    in ``q``, ``k``, ``v``, ``lmk_logw`` and ``w_cont``."""
+    return DSALTTrainFunction.apply(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win, win_edge,
+                                             n_max, cu_list)
+
+
 # --------------------------------------------------------------------------- fused core
 def core_forward(x, gate_weight, gate_bias, n_min, n_max, alpha, q, k, v, k_lmk, cu_seqlens, *, mode="global",
                  block=512, norm_round=False, out_dtype=None, cu_list=None, return_aux=False, workspace=None,

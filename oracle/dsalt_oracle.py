@@ -640,3 +640,98 @@ def attention_backward(q, k, v, out, dout, lse, w, lmk, cu_seqlens, lmk_block=0,
                 d_bias[h, set_id, slots] += rec[nw:]
         set_base += nsets
     return dq, dk, dv, d_bias
+
+
+# --------------------------------------------------------------------------- #
+# training attention with soft selectors -- dsalt/kernels/dsalt_triton_train.py
+# --------------------------------------------------------------------------- #
+def _train_keys(i, L, wc, P, logw_row, win_edge, tau):
+    """Keys of row ``i`` (position in a sequence of length ``L``) with continuous width
+    ``wc``: the band ``0 ≤ d = i − j ≤ w̃`` (``_train_fwd_kernel`` ``:131-141``) with its soft
+    edge bias ``0`` in the core ``d ≤ w̃ − win_edge`` and ``log σ((w̃ − d)/τ)`` outside it,
+    then the landmarks ``p`` with ``0 ≤ p < L``, ``p ≤ i``, ``p < i − w̃`` and log-weight
+    bias (``:173-184``). Returns (positions, bias, is_edge, d_bias/d_w̃, landmark slots)."""
+    j = np.arange(0, i + 1)
+    d = (i - j).astype(F64)
+    band = d <= wc
+    j, d = j[band], d[band]
+    z = (wc - d) / tau
+    core = d <= wc - win_edge
+    bias = np.where(core, 0.0, -np.log1p(np.exp(-z)))
+    dbdw = np.where(core, 0.0, (1.0 - 1.0 / (1.0 + np.exp(-z))) / tau)
+    ok = (P >= 0) & (P < L) & (P <= i) & (P.astype(F64) < i - wc)
+    slots = np.nonzero(ok)[0]
+    pos = np.concatenate([j, P[slots].astype(np.int64)])
+    b = np.concatenate([bias, np.asarray(logw_row, dtype=F64)[slots]])
+    return pos, b, len(j), dbdw, slots
+
+
+def train_attention_forward(q, k, v, lmk, logw, w_cont, cu_seqlens, tau_win, win_edge, scale=None):
+    """``_train_fwd_kernel`` (``dsalt_triton_train.py:74-217``) in float64: softmax over each
+    row's soft band and log-weighted landmarks (one set per sequence), rows with mass ≤ 1e-9
+    zero. Grouped kv heads are indexed. Returns ``(out [T,H,D], lse [T,H])``."""
+    q, k, v = (np.asarray(a, dtype=F64) for a in (q, k, v))
+    T, H, D = q.shape
+    rep = H // k.shape[1]
+    scale = F64(F32(1.0 / math.sqrt(D) if scale is None else scale))
+    wc = np.asarray(w_cont, dtype=F32).astype(F64)
+    out = np.zeros((T, H, D), dtype=F64)
+    lse = np.full((T, H), -np.inf, dtype=F64)
+    for s in range(len(cu_seqlens) - 1):
+        a, b_ = int(cu_seqlens[s]), int(cu_seqlens[s + 1])
+        L = b_ - a
+        for i in range(L):
+            t = a + i
+            for h in range(H):
+                g = h // rep
+                pos, bias, _, _, _ = _train_keys(i, L, wc[t], np.asarray(lmk)[h, s], np.asarray(logw)[h, s],
+                                                 win_edge, tau_win)
+                if pos.size == 0:
+                    continue
+                lg = k[a + pos, g] @ q[t, h] * scale + bias
+                m = lg.max()
+                p = np.exp(lg - m)
+                l = p.sum()
+                if l > 1e-9:
+                    out[t, h] = p @ v[a + pos, g] / l
+                    lse[t, h] = m + math.log(l)
+    return out, lse
+
+
+def train_attention_backward(q, k, v, out, dout, lse, lmk, logw, w_cont, cu_seqlens, tau_win, win_edge,
+                             scale=None):
+    """``_train_bwd_kernel`` / ``_train_bwd_dkdv_kernel`` (``dsalt_triton_train.py:240-490``) in
+    float64: ``p = exp(logit − lse)``, ``ds = p (dO·v − delta)``; ``dq += ds·scale k``,
+    ``dk += ds·scale q``, ``dv += p dO``; ``d_logw[h, s, slot] += ds`` on landmarks;
+    ``d_w̃[i] += Σ ds · (1 − σ(z))/τ`` over the band's edge keys, summed over heads
+    (``:363-376``, ``:688``). Returns ``(dq, dk, dv, d_logw, d_w)``."""
+    q, k, v, out, dout = (np.asarray(a, dtype=F64) for a in (q, k, v, out, dout))
+    lse = np.asarray(lse, dtype=F64)
+    T, H, D = q.shape
+    rep = H // k.shape[1]
+    scale = F64(F32(1.0 / math.sqrt(D) if scale is None else scale))
+    wc = np.asarray(w_cont, dtype=F32).astype(F64)
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    d_logw = np.zeros(np.asarray(logw).shape, dtype=F64)
+    d_w = np.zeros(T, dtype=F64)
+    delta = np.sum(out * dout, axis=-1)
+    for s in range(len(cu_seqlens) - 1):
+        a, b_ = int(cu_seqlens[s]), int(cu_seqlens[s + 1])
+        L = b_ - a
+        for i in range(L):
+            t = a + i
+            for h in range(H):
+                if not np.isfinite(lse[t, h]):
+                    continue
+                g = h // rep
+                pos, bias, nw, dbdw, slots = _train_keys(i, L, wc[t], np.asarray(lmk)[h, s],
+                                                         np.asarray(logw)[h, s], win_edge, tau_win)
+                rows = a + pos
+                p = np.exp(k[rows, g] @ q[t, h] * scale + bias - lse[t, h])
+                ds = p * (v[rows, g] @ dout[t, h] - delta[t, h])
+                dq[t, h] += (ds * scale) @ k[rows, g]
+                np.add.at(dk[:, g], rows, (ds * scale)[:, None] * q[t, h][None, :])
+                np.add.at(dv[:, g], rows, p[:, None] * dout[t, h][None, :])
+                d_logw[h, s, slots] += ds[nw:]
+                d_w[t] += np.sum(ds[:nw] * dbdw)
+    return dq, dk, dv, d_logw, d_w

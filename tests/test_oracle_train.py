@@ -1,0 +1,68 @@
+"""The oracle's soft-selector training attention (``oracle.dsalt_oracle.train_attention_*``,
+a restatement of ``dsalt/kernels/dsalt_triton_train.py``): its backward against float64
+autograd of its forward, in q, k, v, the landmark log-weights and the continuous widths
+(through the soft window edge ``log σ((w̃ − d)/τ)``)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import dsalt_oracle as O
+
+
+def _dense_train_forward(q, k, v, logw, wc, lmk, cu, tau, edge):
+    T, H, D = q.shape
+    rep = H // k.shape[1]
+    scale = float(np.float32(1.0 / math.sqrt(D)))
+    out = torch.zeros_like(q)
+    wcn = wc.detach().numpy()
+    for s in range(len(cu) - 1):
+        a, b = cu[s], cu[s + 1]
+        L = b - a
+        for i in range(L):
+            t = a + i
+            j = np.arange(0, i + 1)
+            d = (i - j).astype(np.float64)
+            band = d <= wcn[t]
+            j, d = j[band], torch.tensor(d[band])
+            core = torch.tensor((d.numpy() <= wcn[t] - edge))
+            z = (wc[t] - d) / tau
+            wbias = torch.where(core, torch.zeros_like(z), torch.nn.functional.logsigmoid(z))
+            for h in range(H):
+                g = h // rep
+                P = lmk[h, s]
+                ok = (P >= 0) & (P < L) & (P <= i) & (P.astype(np.float64) < i - wcn[t])
+                slots = np.nonzero(ok)[0]
+                rows = np.concatenate([a + j, a + P[slots]])
+                lg = k[rows, g] @ q[t, h] * scale
+                lg = lg + torch.cat([wbias, logw[h, s, slots]])
+                out[t, h] = torch.softmax(lg, 0) @ v[rows, g]
+    return out
+
+
+@pytest.mark.parametrize("H,Hkv", [(2, 2), (4, 2)])
+def test_oracle_train_backward_matches_autograd(H, Hkv):
+    rng = np.random.default_rng(11)
+    cu = [0, 90, 150]
+    T, D, k_lmk, tau, edge = cu[-1], 8, 5, 1.0, 4
+    q = rng.standard_normal((T, H, D))
+    k = rng.standard_normal((T, Hkv, D))
+    v = rng.standard_normal((T, Hkv, D))
+    wc = (rng.uniform(2.0, 30.0, T)).astype(np.float32)
+    lmk = np.full((H, 2, k_lmk), -1, dtype=np.int32)
+    for h in range(H):
+        for s in range(2):
+            lmk[h, s, :k_lmk - 1] = rng.choice(55, size=k_lmk - 1, replace=False)  # any slot order
+    logw = rng.standard_normal(lmk.shape) * 0.5
+    out, lse = O.train_attention_forward(q, k, v, lmk, logw, wc, cu, tau, edge)
+    dout = rng.standard_normal(out.shape)
+    dq, dk, dv, dlw, dw = O.train_attention_backward(q, k, v, out, dout, lse, lmk, logw, wc, cu, tau, edge)
+    tq, tk, tv = (torch.tensor(a, requires_grad=True) for a in (q, k, v))
+    tl = torch.tensor(logw, requires_grad=True)
+    tw = torch.tensor(wc.astype(np.float64), requires_grad=True)
+    o = _dense_train_forward(tq, tk, tv, tl, tw, lmk, cu, tau, edge)
+    np.testing.assert_allclose(o.detach().numpy(), out, atol=1e-12)
+    (o * torch.tensor(dout)).sum().backward()
+    for got, ref in ((dq, tq.grad), (dk, tk.grad), (dv, tv.grad), (dlw, tl.grad), (dw, tw.grad)):
+        np.testing.assert_allclose(got, ref.numpy(), atol=1e-10)
