@@ -1,6 +1,6 @@
 """``DSALTAttention`` with the reference's constructor, parameters and forward signature
-(``dsalt/modules/dsalt_attention.py:147-369``), whose packed inference path runs on the
-B200 kernels of this package.
+(``dsalt/modules/dsalt_attention.py:147-369``), whose packed path (inference and
+training) runs on the B200 kernels of this package.
 
 Same state-dict keys (``q_proj``, ``k_proj``, ``v_proj``, ``out_proj``, ``win_gate``,
 ``alpha_w``), same RoPE cache and half-split rotation, same ``(out, aux)`` return. The
@@ -19,7 +19,17 @@ mask, softmax of the masked scores in the caller's dtype). As in the reference i
 collected unless ``_collect_last_P`` is set to False; it costs O(T0²) memory, so callers
 that need only the output (the decoder stack in :mod:`dsalt_b200.model`) turn it off.
 
-Out of scope (raise): the training path and the batched ``[B, T, d]`` path.
+In training mode the packed path is the reference's Triton training branch
+(``_packed_train_triton`` / ``_train_selectors``, ``:438-487``): continuous widths
+``w̃ = n_min + σ(win_gate(x))·(n_max − n_min)``, landmarks selected without gradient on
+``floor(w̃)`` by the global selection, their log-weights ``log σ(s/τ_lmk)`` from the hybrid
+scores (differentiable in ``alpha_w``, ``x`` and ``v_proj``), and the soft-selector attention
+of :func:`dsalt_b200.ops.dsalt_train_attention`, whose backward carries the gradients of the
+soft window edge to ``win_gate`` and of the landmark weights to ``alpha_w``.
+
+Out of scope (raise): the batched ``[B, T, d]`` path, and training with
+``selection="block_causal"`` (the training kernel takes one landmark set per sequence, as
+the reference's does).
 """
 from __future__ import annotations
 
@@ -31,6 +41,22 @@ import torch.nn.functional as F
 
 from . import library  # noqa: F401  (registers torch.ops.dsalt_b200.*)
 from . import ops
+
+
+def hybrid_scores_per_head(x, W_V, alpha, n_heads, dh):
+    """Per-head hybrid score ``α·z_v + (1 − α)·z_x`` over all ``T`` rows of ``x``
+    (``dsalt/kernels/landmark_tokens_ker.py:19-61``), differentiable in ``x``, ``W_V`` and
+    ``alpha``: the training path's landmark weights. The hard selection uses the CUDA
+    selection kernels instead."""
+    T = x.shape[0]
+    x_norm = x.norm(dim=-1).float()
+    z_x = (x_norm - x_norm.mean()) / x_norm.std().clamp(min=1e-6)
+    n_kv = W_V.shape[0] // dh
+    xwv = (x @ W_V.T).view(T, n_kv, dh).norm(dim=-1).float()
+    z_v = (xwv - xwv.mean(0, keepdim=True)) / xwv.std(0, keepdim=True).clamp(min=1e-6)
+    if n_kv != n_heads:
+        z_v = z_v.repeat_interleave(n_heads // n_kv, dim=1)
+    return alpha * z_v + (1.0 - alpha) * z_x.unsqueeze(1)
 
 
 def build_rope_cache(seq_len, head_dim, device, dtype=torch.float32, base=10000.0, scale=1.0):
@@ -92,7 +118,8 @@ class DSALTAttention(nn.Module):
         return torch.sigmoid(self.alpha_w)
 
     def forward(self, x, cu_seqlens=None, max_seqlen=None, rope_cs=None, cu_list=None):
-        """Packed inference forward ``-> (out [T, d_model], aux 0)``. ``max_seqlen`` is
+        """Packed forward ``-> (out [T, d_model], aux 0)``: the inference kernels in eval
+        mode, the differentiable soft-selector attention in training mode. ``max_seqlen`` is
         accepted for signature compatibility and not needed: the kernels derive every
         sequence length from ``cu_seqlens`` (or ``cu_list``). Under ``torch.compile`` pass
         ``cu_list`` (the host list of ``cu_seqlens``): reading it from the device tensor is a
@@ -100,13 +127,12 @@ class DSALTAttention(nn.Module):
         if cu_seqlens is None:
             raise NotImplementedError("dsalt_b200 implements the packed path; pass cu_seqlens")
         if self.training:
-            raise NotImplementedError("dsalt_b200 implements the inference forward; call .eval()")
+            return self._packed_train(x, cu_seqlens, x.shape[0], x.device, rope_cs, cu_list)
         return self._packed(x, cu_seqlens, x.shape[0], x.device, rope_cs, cu_list)
 
-    @torch.no_grad()
-    def _packed(self, x, cu_seqlens, total_len, device, rope_cs=None, cu_list=None):
+    def _qkv(self, x, cu_h, total_len, device, rope_cs):
+        """Projections and RoPE (``_packed`` ``:566-589``); kv heads stay grouped."""
         T, H, Hkv, D = total_len, self.n_heads, self.n_kv_heads, self.head_dim
-        cu_h = ops._host_cu(cu_seqlens, cu_list)
         q = self.q_proj(x).view(T, H, D)
         k = self.k_proj(x).view(T, Hkv, D)
         v = self.v_proj(x).view(T, Hkv, D)
@@ -117,6 +143,47 @@ class DSALTAttention(nn.Module):
             cos, sin = rope_cs
         cos, sin = cos.to(q.dtype), sin.to(q.dtype)
         q, k = apply_rotary_emb(q, k, cos.unsqueeze(1), sin.unsqueeze(1))
+        return q, k, v
+
+    def _packed_train(self, x, cu_seqlens, total_len, device, rope_cs=None, cu_list=None):
+        """Training forward (``_packed`` ``:596-605`` → ``_packed_train_triton`` ``:438-455``)."""
+        if self.selection != "global":
+            raise NotImplementedError("training takes one landmark set per sequence: selection='global'")
+        T = total_len
+        cu_h = ops._host_cu(cu_seqlens, cu_list)
+        q, k, v = self._qkv(x, cu_h, T, device, rope_cs)
+        w_cont, lmk_pos, lmk_logw = self._train_selectors(x, cu_seqlens, T, cu_h)
+        out = ops.dsalt_train_attention(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_win=self.tau_win,
+                                        win_edge=float(self.win_edge), n_max=self.n_max, cu_list=cu_h)
+        self._last_P = None
+        aux = torch.zeros((), device=x.device, dtype=x.dtype)
+        return self.out_proj(out.view(T, self.d_model).to(self.out_proj.weight.dtype)), aux
+
+    def _train_selectors(self, x, cu_seqlens, total_len, cu_h):
+        """``(w_cont [T], lmk_pos [H, S, k], lmk_logw [H, S, k])`` (``_train_selectors``
+        ``:457-487``): the continuous widths and the landmark log-weights carry gradients, the
+        landmark positions do not."""
+        H, D = self.n_heads, self.head_dim
+        w_cont = self.n_min + torch.sigmoid(self.win_gate(x).squeeze(-1)) * (self.n_max - self.n_min)
+        alpha = self._alpha()
+        with torch.no_grad():
+            w_disc = w_cont.floor().clamp(min=1)
+            lmk_pos, _, _ = ops.compute_landmark_indices(x.detach(), self.v_proj.weight.detach(),
+                                                         alpha.detach().float(), w_disc, cu_seqlens, self.k_lmk,
+                                                         self.n_min, total_len, cu_h, head_dim=D)
+        scores = hybrid_scores_per_head(x, self.v_proj.weight, alpha, H, D)              # [T, H]
+        starts = torch.tensor(cu_h[:-1], dtype=torch.long, device=x.device)
+        abs_pos = starts[None, :, None] + lmk_pos.clamp(min=0)                           # [H, S, k]
+        s_sel = scores[abs_pos, torch.arange(H, device=x.device)[:, None, None]]
+        lmk_logw = torch.log(torch.sigmoid(s_sel / self.tau_lmk).clamp(min=1e-20))
+        lmk_logw = torch.where(lmk_pos >= 0, lmk_logw, torch.full_like(lmk_logw, float("-inf")))
+        return w_cont, lmk_pos, lmk_logw
+
+    @torch.no_grad()
+    def _packed(self, x, cu_seqlens, total_len, device, rope_cs=None, cu_list=None):
+        T, H, Hkv, D = total_len, self.n_heads, self.n_kv_heads, self.head_dim
+        cu_h = ops._host_cu(cu_seqlens, cu_list)
+        q, k, v = self._qkv(x, cu_h, T, device, rope_cs)
         amp = torch.is_autocast_enabled("cuda") if x.is_cuda else False
         # the width logit comes from the same library op as the reference's
         # _window_continuous (win_gate(x), :275), so that the widths equal the reference's

@@ -2,6 +2,8 @@
 ``dsalt/kernels/dsalt_triton_train.py``) against the float64 oracle
 (``oracle.dsalt_oracle.train_attention_*``, itself checked against autograd in
 ``tests/test_oracle_train.py``), and the autograd function built on them."""
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -95,3 +97,94 @@ def test_train_autograd_function():
         _check(got.float().cpu().numpy(), r, 2 ** -7, name)
     _check(tl.grad.cpu().numpy(), ref[3], 2e-4, "d_logw")
     _check(tw.grad.cpu().numpy(), ref[4], 2e-4, "d_w")
+
+
+def _dense_module_train(m, x, cu, lmk_pos, w_gpu):
+    """Float64 dense restatement of the module's training forward (``_packed_train_triton`` with
+    ``_train_selectors``, ``dsalt_attention.py:438-487``, and the kernel's bias
+    ``_dense_logbias_from_kernel`` ``:513-563``) on the same landmark positions. The hard masks
+    (band ``d ≤ w̃``, core ``d ≤ w̃ − win_edge``, landmark ``p < i − w̃``) use the GPU's fp32
+    widths ``w_gpu`` so that a width within rounding of an integer cannot flip a mask; the soft
+    biases use the float64 widths, so their gradients flow."""
+    from dsalt_b200.module import hybrid_scores_per_head
+    T = x.shape[0]
+    H, Hkv, D = m.n_heads, m.n_kv_heads, m.head_dim
+    q, k, v = m._qkv(x, cu, T, x.device, None)
+    w64 = m.n_min + torch.sigmoid(m.win_gate(x).squeeze(-1)) * (m.n_max - m.n_min)
+    scores = hybrid_scores_per_head(x, m.v_proj.weight, m._alpha(), H, D)
+    outs = []
+    for s in range(len(cu) - 1):
+        a, b = cu[s], cu[s + 1]
+        L = b - a
+        i = torch.arange(L, dtype=torch.float64)[:, None]
+        d = i - torch.arange(L, dtype=torch.float64)[None, :]
+        wf, wd = w_gpu[a:b, None], w64[a:b, None]
+        band = (d >= 0) & (d <= wf)
+        core = d <= wf - m.win_edge
+        wb = torch.where(core, torch.zeros_like(d), torch.log(torch.sigmoid((wd - d) / m.tau_win).clamp(min=1e-20)))
+        wb = wb.masked_fill(~band, float("-inf"))
+        heads = []
+        for h in range(H):
+            g = h // (H // Hkv)
+            p = lmk_pos[h, s]
+            pc = p.clamp(min=0)
+            logw = torch.log(torch.sigmoid(scores[a + pc, h] / m.tau_lmk).clamp(min=1e-20))
+            pf = pc.double()[None, :]
+            ok = (p >= 0)[None, :] & (pf <= i) & (pf < i - wf)
+            lb = torch.where(ok, logw[None, :], torch.full_like(pf.expand(L, -1), float("-inf")))
+            lg = torch.cat([q[a:b, h] @ k[a:b, g].T / math.sqrt(D) + wb, q[a:b, h] @ k[a + pc, g].T / math.sqrt(D) + lb], 1)
+            heads.append(torch.softmax(lg, 1) @ torch.cat([v[a:b, g], v[a + pc, g]], 0))
+        outs.append(torch.stack(heads, 1))
+    return m.out_proj(torch.cat(outs, 0).reshape(T, m.d_model))
+
+
+def test_module_training_matches_dense():
+    """``DSALTAttention`` in training mode: output and the gradients of every parameter
+    (``win_gate`` through the soft window edge, ``alpha_w`` through the landmark weights)
+    against the float64 dense restatement."""
+    import copy
+    from dsalt_b200 import ops
+    from dsalt_b200.module import DSALTAttention
+    dev = _dev()
+    torch.manual_seed(0)
+    m = DSALTAttention(d_model=256, n_heads=4, n_min=8, n_max=64, k_lmk=8, max_seq_len=512, n_kv_heads=2).to(dev)
+    with torch.no_grad():
+        m.win_gate.weight.mul_(4.0)  # spread the widths over [n_min, n_max]
+    m.train()
+    cu = [0, 200, 330]
+    x = torch.randn(cu[-1], 256, device=dev)
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    out, aux = m(x, cu_t, cu_list=cu)
+    gout = torch.randn(out.shape, generator=torch.Generator().manual_seed(1)).to(dev)
+    out.backward(gout)
+    with torch.no_grad():
+        w_gpu = m.n_min + torch.sigmoid(m.win_gate(x).squeeze(-1)) * (m.n_max - m.n_min)
+        lmk_pos, _, _ = ops.compute_landmark_indices(x, m.v_proj.weight, m._alpha().float(), w_gpu.floor().clamp(min=1),
+                                                     cu_t, m.k_lmk, m.n_min, cu[-1], cu, head_dim=m.head_dim)
+    mc = copy.deepcopy(m).cpu().double()
+    mc.zero_grad()
+    ref = _dense_module_train(mc, x.cpu().double(), cu, lmk_pos.cpu(), w_gpu.cpu().double())
+    _check(out.detach().cpu().double().numpy(), ref.detach().numpy(), 1e-4, "out")
+    ref.backward(gout.cpu().double())
+    for (name, p), (_, pc) in zip(m.named_parameters(), mc.named_parameters()):
+        r = pc.grad.numpy()
+        err = float(np.abs(p.grad.double().cpu().numpy() - r).max())
+        assert err <= 1e-3 * float(np.abs(r).max()) + 1e-6, f"grad {name}: {err:.3e} vs max {np.abs(r).max():.3e}"
+    assert float(m.alpha_w.grad.abs().max()) > 0 and float(m.win_gate.weight.grad.abs().max()) > 0
+
+
+def test_module_training_bf16_autocast():
+    """Training step under bf16 autocast (the trainer's setting): finite loss and gradients."""
+    from dsalt_b200.module import DSALTAttention
+    dev = _dev()
+    torch.manual_seed(2)
+    m = DSALTAttention(d_model=512, n_heads=8, n_min=16, n_max=128, k_lmk=16, max_seq_len=2048).to(dev).train()
+    cu = [0, 700, 1024, 1500]
+    x = torch.randn(cu[-1], 512, device=dev)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out, _ = m(x, torch.tensor(cu, dtype=torch.int32, device=dev), cu_list=cu)
+        loss = out.float().pow(2).mean()
+    loss.backward()
+    assert torch.isfinite(loss)
+    for name, p in m.named_parameters():
+        assert p.grad is not None and torch.isfinite(p.grad).all(), name
