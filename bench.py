@@ -506,6 +506,80 @@ def run_backward(args):
                       "device_status": ops.device_status()}), flush=True)
 
 
+def run_train(args):
+    """The soft-selector training attention (``dsalt_train_attention``, the reference's
+    ``dsalt_triton_train_attention``) forward and backward at BASELINE configs[1]'s shapes, the
+    pack a training step sees: 4 sequences of 8192 packed, H = 12, D = 64, bf16, k = 64 landmarks
+    per (head, sequence) from the global selection, continuous widths
+    ``16 + σ(l)·(256 − 16)`` with ``l ~ N(0, 1.5)``, log-weights ``log σ(N(0, 1))``. A step is
+    one forward (out, lse) and one backward (dq, dk, dv, d_logw, d_w) through the C ABI;
+    ``value`` counts query rows per second over both. ``useful_tflops`` counts two length-D
+    products per (query, key) pair in the forward and five in the backward."""
+    from dsalt_b200 import ops
+    dev = torch.device("cuda", 0)
+    S, Ls, H, D, k = 4, 8192, 12, 64, 64
+    T = S * Ls
+    g = torch.Generator(device=dev).manual_seed(0)
+    q, kk, v = (torch.randn(T, H, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+    w = 16.0 + torch.sigmoid(1.5 * torch.randn(T, device=dev, generator=g)) * (256.0 - 16.0)
+    cu = [s * Ls for s in range(S + 1)]
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    x = torch.randn(T, 768, device=dev, generator=g).to(torch.bfloat16)
+    wv = (0.02 * torch.randn(H * D, 768, device=dev, generator=g)).to(torch.bfloat16)
+    alpha = torch.full((H,), 0.6, device=dev)
+    lmk, _, _ = ops.compute_landmark_indices(x, wv, alpha, w.floor().clamp(min=1), cu_t, k, 16, T, cu, head_dim=D)
+    logw = torch.nn.functional.logsigmoid(torch.randn(H, S, k, device=dev, generator=g))
+    dout = torch.randn(T, H, D, device=dev, generator=g)
+    tau, edge = 1.0, 4.0
+
+    def fwd():
+        return ops.train_attention_forward(q, kk, v, lmk, logw, w, cu_t, tau, edge, out_dtype=torch.float32, cu_list=cu)
+
+    out, lse = fwd()
+
+    def bwd():
+        return ops.train_attention_backward(dout, q, kk, v, out, lse, lmk, logw, w, cu_t, tau, edge, cu_list=cu)
+
+    for _ in range(args.warmup):
+        fwd()
+        bwd()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with ClockSampler(0) as clk:
+        ms_f = ms_b = 0.0
+        for _ in range(args.steps):
+            ev[0].record()
+            fwd()
+            ev[1].record()
+            bwd()
+            ev[2].record()
+            torch.cuda.synchronize()
+            ms_f += ev[0].elapsed_time(ev[1])
+            ms_b += ev[1].elapsed_time(ev[2])
+    ms_f, ms_b = ms_f / args.steps, ms_b / args.steps
+    i = torch.arange(Ls, device=dev).repeat(S)
+    band = int(torch.minimum(w.floor().long(), i).sum() + T)
+    pos = lmk.long()
+    lmk_pairs = 0
+    for s in range(S):  # landmark p serves the queries i > p + w̃(i) of its sequence; count them per head
+        rows = torch.arange(Ls, device=dev)
+        lim = rows.double() - w[cu[s]:cu[s + 1]].double()
+        srt = torch.sort(lim).values
+        p = pos[:, s][pos[:, s] >= 0].double()
+        lmk_pairs += int((Ls - torch.searchsorted(srt, p, right=True)).sum())
+    pairs = band * H + lmk_pairs
+    ms = ms_f + ms_b
+    print(json.dumps({"metric": "DSALT training attention fwd+bwd query rows/s", "value": T / (ms / 1e3),
+                      "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                      "ms_forward": ms_f, "ms_backward": ms_b, "higher_is_better": True,
+                      "dtype": "bf16 inputs, fp32 arithmetic", "data": "synthetic",
+                      "config": {"workload": f"dsalt_train_attn_S{S}x{Ls}_H{H}_D{D}_k{k}_wmax256", "L": T},
+                      "pairs_per_step": pairs,
+                      "useful_tflops_forward": pairs * 2 * 2 * D / ms_f / 1e9,
+                      "useful_tflops_backward": pairs * 5 * 2 * D / ms_b / 1e9, "clocks": clk.summary(),
+                      "device_status": ops.device_status()}), flush=True)
+
+
 def run_prefill(args):
     """Full-model prefill on one GPU: random-init bf16
     weights, uniform random token ids from a seed, every layer's attention on this
@@ -557,9 +631,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="core", choices=["core", "backward", *PREFILL],
+    ap.add_argument("--workload", default="core", choices=["core", "backward", "train", *PREFILL],
                     help="core: the DSALT attention core (the benchmark); backward: the attention backward on the "
-                         "core's inputs; prefill_cfg3 / prefill_cfg5: full-model prefill of BASELINE configs[2] / "
+                         "core's inputs; train: the soft-selector training attention forward + backward at "
+                         "configs[1]'s shapes; prefill_cfg3 / prefill_cfg5: full-model prefill of BASELINE configs[2] / "
                          "configs[4] on one GPU")
     ap.add_argument("--seq-len", type=int, default=CFG["L"],
                     help="sequence length (131072 is the benchmark; shorter ones for profiler captures)")
@@ -572,6 +647,9 @@ def main():
     if args.workload == "backward":
         args.warmup = max(args.warmup, 3)
         return run_backward(args)
+    if args.workload == "train":
+        args.warmup = max(args.warmup, 3)
+        return run_train(args)
     if args.workload != "core":
         args.warmup = max(args.warmup, 3)
         return run_prefill(args)
