@@ -42,8 +42,9 @@ SIGNATURES = {
     "dsalt_attention_bwd_workspace_bytes": (_SZ, [_I64, _I]),
     "dsalt_attention_bwd": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _I, _P, _I, _P, _P, _P, _P, _I, _I,
                                  _I, _P, _I, _P, _P, _P, _P, _P, _SZ, _P]),
+    "dsalt_train_attention_fwd_workspace_bytes": (_SZ, [_I64, _I, _I, _I]),
     "dsalt_train_attention_fwd": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P, _I, _P, _I, _F, _F,
-                                       _P, _I, _P, _P]),
+                                       _P, _I, _P, _P, _SZ, _P]),
     "dsalt_train_attention_bwd": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _I, _P, _I, _P, _P, _P, _P,
                                        _I, _P, _I, _F, _F, _P, _P, _P, _P, _P, _P, _SZ, _P]),
     "dsalt_attention_fwd_noalloc": (_I, [_P, _P, _P, _I, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P, _I, _I, _P, _I,

@@ -89,6 +89,10 @@ struct Params {
   int shard_tiles, n_sets_local;
   float scale_log2;  // log2(e) / sqrt(head_dim)
   float inv_scale;   // sqrt(head_dim): landmark bias in raw-logit units
+  // soft window edge (training forward, SOFT kernels): continuous widths w̃ (w then holds
+  // floor(w̃) + 1), edge width (≤ 4) and temperature
+  const float* w_soft;
+  float soft_edge, soft_tau;
   uint32_t idesc_qk, idesc_pv;
   void* out;
   int out_dtype;
@@ -353,7 +357,7 @@ __device__ __forceinline__ uint32_t pack_p(bool bf, float lo, float hi) {
   return bf ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
 }
 
-template <int HD, bool BF>
+template <int HD, bool BF, bool SOFT>
 __global__ void __launch_bounds__(Pipes<HD>::THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_lk,
@@ -653,9 +657,29 @@ __global__ void __launch_bounds__(Pipes<HD>::THREADS, 1)
       // so as unsigned values non-decreasing, and the landmarks the row may use
       // (0 <= p < min(L, i-w+1)) are a prefix of the set
       int lo, lcnt;
+      // soft edge (SOFT): the first ne band columns from lo_raw, i.e. d = i - j from floor(w̃)
+      // down, get log σ((w̃ - d)/τ) in raw-logit units eb0..eb3
+      int lo_raw, ne = 0;
+      float eb0 = 0.0f, eb1 = 0.0f, eb2 = 0.0f, eb3 = 0.0f;
       {
-        const int wi = max(S.wv[r], 1);
-        const int lo_raw = i - wi + 1;
+        const int wi = SOFT ? S.wv[r] : max(S.wv[r], 1);  // SOFT: width 0 = no band (w̃ < 0)
+        lo_raw = i - wi + 1;
+        if constexpr (SOFT) {
+          if (vrow && wi > 0) {
+            const float wc = __ldg(p.w_soft + f.wb + i);
+            const int dhi = wi - 1;  // floor(w̃)
+            const int dlo = max(0, (int)floorf(wc - p.soft_edge) + 1);  // core: d <= w̃ - edge
+            ne = min(dhi - dlo + 1, 4);
+            auto eb = [&](int kk) {
+              const float z = (wc - (float)(dhi - kk)) / p.soft_tau;
+              return -logf(1.0f + expf(-z)) * p.inv_scale;
+            };
+            if (ne > 0) eb0 = eb(0);
+            if (ne > 1) eb1 = eb(1);
+            if (ne > 2) eb2 = eb(2);
+            if (ne > 3) eb3 = eb(3);
+          }
+        }
         lo = vrow ? max(lo_raw, 0) : 0x3fffffff;
         const unsigned lim = vrow ? (unsigned)max(0, min(f.L, lo_raw)) : 0u;
         int a0 = 0, a1 = p.k_lmk;
@@ -700,6 +724,28 @@ __global__ void __launch_bounds__(Pipes<HD>::THREADS, 1)
             const float bq = idx < p.k_lmk ? __ldg(Bset + idx) * p.inv_scale : 0.0f;
 #pragma unroll
             for (int e = 0; e < 32; ++e) x[q * 32 + e] += __shfl_sync(0xffffffffu, bq, e);
+          }
+        }
+        if constexpr (SOFT) {
+          if (is_w) {
+            // columns ea .. ea + ne - 1 of this tile carry the soft edge; only the chunks that
+            // hold one of some lane's edge columns are visited (warp-uniform)
+            const int ea = lo_raw - kb;
+            uint32_t touch_l = 0;
+#pragma unroll
+            for (int cc = 0; cc < BN / 32; ++cc)
+              touch_l |= (uint32_t)(ne > 0 && ea <= cc * 32 + 31 && ea + ne - 1 >= cc * 32) << cc;
+            const uint32_t touch = __reduce_or_sync(0xffffffffu, touch_l);
+#pragma unroll
+            for (int cc = 0; cc < BN / 32; ++cc) {
+              if (!((touch >> cc) & 1)) continue;
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                const int kk = cc * 32 + e - ea;
+                const float bv = kk == 0 ? eb0 : (kk == 1 ? eb1 : (kk == 2 ? eb2 : eb3));
+                x[cc * 32 + e] += (unsigned)kk < (unsigned)ne ? bv : 0.0f;
+              }
+            }
           }
         }
         uint64_t s0 = pk2(0.f, 0.f), s1 = s0;
@@ -952,8 +998,11 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
                    int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, int32_t* set_base, int32_t* tile_base,
                    int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
-                   cudaStream_t stream, const ShardArgs* shard) {
+                   cudaStream_t stream, const ShardArgs* shard, const float* w_soft, float soft_edge,
+                   float soft_tau) {
   using namespace tc;
+  if (w_soft && (shard || !(soft_edge >= 0.0f && soft_edge <= 4.0f) || !(soft_tau > 0.0f)))
+    return fail(DSALT_ERR_UNSUPPORTED, "attention (tensor cores): soft edge needs 0 <= win_edge <= 4, tau > 0");
   if (HD != 64 && HD != 128)
     return fail(DSALT_ERR_UNSUPPORTED, "attention (tensor cores): head_dim %d not supported (64, 128)", HD);
   if (k_lmk > MAX_LMK) return fail(DSALT_ERR_UNSUPPORTED, "attention: k_lmk %d above %d", k_lmk, MAX_LMK);
@@ -1022,6 +1071,9 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
       if ((rc = make_map(&mlv, shard->lmk_tiles_v, dtype, HD, 1, tiles * BN, HD))) return rc;
     }
   }
+  p.w_soft = w_soft;
+  p.soft_edge = soft_edge;
+  p.soft_tau = soft_tau;
   p.scale_log2 = (float)(1.0 / sqrt((double)HD) * 1.4426950408889634);
   p.inv_scale = (float)sqrt((double)HD);
   const uint32_t ab = dtype == DSALT_BF16 ? 1u : 0u;
@@ -1043,8 +1095,10 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
   const size_t smem = (HD == 64 ? Smem<64>::BYTES : Smem<128>::BYTES) + 1024;
   const int threads = HD == 64 ? Pipes<64>::THREADS : Pipes<128>::THREADS;
   const bool bf = dtype == DSALT_BF16;
-  auto kern = HD == 64 ? (bf ? attn_fwd_tc_kernel<64, true> : attn_fwd_tc_kernel<64, false>)
-                       : (bf ? attn_fwd_tc_kernel<128, true> : attn_fwd_tc_kernel<128, false>);
+  auto kern = w_soft ? (HD == 64 ? (bf ? attn_fwd_tc_kernel<64, true, true> : attn_fwd_tc_kernel<64, false, true>)
+                                 : (bf ? attn_fwd_tc_kernel<128, true, true> : attn_fwd_tc_kernel<128, false, true>))
+                     : (HD == 64 ? (bf ? attn_fwd_tc_kernel<64, true, false> : attn_fwd_tc_kernel<64, false, false>)
+                                 : (bf ? attn_fwd_tc_kernel<128, true, false> : attn_fwd_tc_kernel<128, false, false>));
   if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "attention smem attr")))
     return rc;

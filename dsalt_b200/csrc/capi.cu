@@ -39,7 +39,10 @@ int launch_attn_tc(const void* q, const void* k, const void* v, int dtype, int64
                    int64_t q_stride, int64_t kv_stride, const int32_t* w, const int32_t* lmk, const float* lmk_bias,
                    int k_lmk, int lmk_block, const int32_t* cu, int n_seqs, int32_t* set_base, int32_t* tile_base,
                    int4* plan, int64_t max_tiles, void* out, int out_dtype, float* lse, int* err,
-                   cudaStream_t stream, const ShardArgs* shard = nullptr);
+                   cudaStream_t stream, const ShardArgs* shard = nullptr, const float* w_soft = nullptr,
+                   float soft_edge = 0.f, float soft_tau = 1.f);
+int launch_train_prep(const float* w_cont, int64_t T, const int32_t* lmk, const float* logw, int64_t n_sets,
+                      int k_lmk, int32_t* w_int, int32_t* lmk_sorted, float* logw_sorted, cudaStream_t stream);
 int launch_chunk_table(const int32_t* cu, int n_seqs, int C, int32_t* base, cudaStream_t stream);
 size_t attention_bwd_workspace_bytes(int n_seqs);
 int launch_attn_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int H, int Hkv, int HD,
@@ -224,22 +227,56 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
                         out_dtype, lse, device_status_ptr(), s);
 }
 
+// attention workspace | integer widths [T] | sorted sets [H, S, k] | their log-weights
+size_t dsalt_train_attention_fwd_workspace_bytes(int64_t T, int n_heads, int n_seqs, int k_lmk) {
+  if (n_seqs < 1 || T < 0 || n_heads < 1 || k_lmk < 0) return 0;
+  const size_t sets = (size_t)n_heads * n_seqs * k_lmk;
+  return dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k_lmk, 0) + a256(4 * (size_t)T) + 2 * a256(4 * sets);
+}
+
 int dsalt_train_attention_fwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads,
                               int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, const float* w_cont,
                               const int32_t* lmk, const float* lmk_logw, int k_lmk, const int32_t* cu_seqlens,
                               int n_seqs, float tau_win, float win_edge, void* out, int out_dtype, float* lse,
-                              void* stream) {
+                              void* workspace, size_t workspace_bytes, void* stream) {
   if (T < 0 || n_heads < 1 || n_kv < 1 || n_heads % n_kv || n_seqs < 1 || k_lmk < 0 || !(tau_win > 0.f))
     return fail(DSALT_ERR_INVALID, "training attention: bad sizes");
   if (!valid_dtype(dtype) || !valid_dtype(out_dtype)) return fail(DSALT_ERR_INVALID, "training attention: dtype");
   if (q_stride < (int64_t)n_heads * head_dim || kv_stride < (int64_t)n_kv * head_dim)
     return fail(DSALT_ERR_INVALID, "training attention: token stride smaller than heads x head_dim");
   if (T == 0) return DSALT_OK;
-  if (!q || !k || !v || !w_cont || !cu_seqlens || !out || (k_lmk > 0 && (!lmk || !lmk_logw)))
+  if (!q || !k || !v || !w_cont || !cu_seqlens || !out || (k_lmk > 0 && (!lmk || !lmk_logw)) || !workspace)
     return fail(DSALT_ERR_INVALID, "training attention: null pointer");
-  return launch_train_fwd(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w_cont, lmk, lmk_logw,
-                          k_lmk, cu_seqlens, n_seqs, tau_win, win_edge, out, out_dtype, lse,
-                          reinterpret_cast<cudaStream_t>(stream));
+  if (T > 0x7fffff00LL) return fail(DSALT_ERR_UNSUPPORTED, "training attention: T too large");
+  const size_t need = dsalt_train_attention_fwd_workspace_bytes(T, n_heads, n_seqs, k_lmk);
+  if (workspace_bytes < need)
+    return fail(DSALT_ERR_WORKSPACE, "training attention: workspace %zu < %zu", workspace_bytes, need);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // bf16 / fp16 with edge widths up to 4 (the reference's default is 4): the tensor-core
+  // kernel's soft-edge mode; otherwise the CUDA-core kernel
+  const bool tc = dtype != DSALT_F32 && (head_dim == 64 || head_dim == 128) && win_edge >= 0.f && win_edge <= 4.f &&
+                  k_lmk <= 256 && !(((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15) &&
+                  (q_stride * 2) % 16 == 0 && (kv_stride * 2) % 16 == 0;
+  if (!tc)
+    return launch_train_fwd(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w_cont, lmk, lmk_logw,
+                            k_lmk, cu_seqlens, n_seqs, tau_win, win_edge, out, out_dtype, lse, s);
+  char* ws = reinterpret_cast<char*>(workspace);
+  const size_t table_bytes = a256(sizeof(int32_t) * (size_t)(n_seqs + 1));
+  int32_t* set_base = reinterpret_cast<int32_t*>(ws);
+  int32_t* tile_base = reinterpret_cast<int32_t*>(ws + table_bytes);
+  int4* plan = reinterpret_cast<int4*>(ws + 2 * table_bytes);
+  char* tail = ws + dsalt_attention_workspace_bytes(T, n_seqs, n_heads, k_lmk, 0);
+  const size_t sets = (size_t)n_heads * n_seqs * k_lmk;
+  int32_t* w_int = reinterpret_cast<int32_t*>(tail);
+  int32_t* lmk_sorted = reinterpret_cast<int32_t*>(tail + a256(4 * (size_t)T));
+  float* logw_sorted = reinterpret_cast<float*>(tail + a256(4 * (size_t)T) + a256(4 * sets));
+  int rc = launch_train_prep(w_cont, T, lmk, lmk_logw, (int64_t)n_heads * n_seqs, k_lmk, w_int, lmk_sorted,
+                             logw_sorted, s);
+  if (rc) return rc;
+  return launch_attn_tc(q, k, v, dtype, T, n_heads, n_kv, head_dim, q_stride, kv_stride, w_int,
+                        k_lmk > 0 ? lmk_sorted : nullptr, k_lmk > 0 ? logw_sorted : nullptr, k_lmk, 0, cu_seqlens,
+                        n_seqs, set_base, tile_base, plan, attention_max_tiles(T, n_seqs), out, out_dtype, lse,
+                        device_status_ptr(), s, nullptr, w_cont, win_edge, tau_win);
 }
 
 int dsalt_train_attention_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,

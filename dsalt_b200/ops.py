@@ -320,7 +320,9 @@ def train_attention_forward(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_
     ``dsalt/kernels/dsalt_triton_train.py:74-217``): ``(out [T,H,D], lse [T,H])``. ``w_cont [T]``
     continuous widths, ``lmk_pos [H, S, k]`` one landmark set per sequence (any order, ``-1``
     = none), ``lmk_logw [H, S, k]`` their log-weights. ``out`` is in ``out_dtype`` (default:
-    the input dtype)."""
+    the input dtype). bf16 / fp16 inputs with ``win_edge <= 4`` run on the tensor cores (P
+    rounded to the input dtype for P·V, as the reference's ``tl.dot``), fp32 inputs on CUDA
+    cores in fp32."""
     _cuda(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens)
     T, H, D = q.shape
     n_kv = k.shape[1]
@@ -330,10 +332,11 @@ def train_attention_forward(q, k, v, lmk_pos, lmk_logw, w_cont, cu_seqlens, tau_
     kl = int(lmk_pos.shape[-1])
     out = torch.empty(T, H, D, dtype=out_dtype or q.dtype, device=q.device)
     lse = torch.empty(T, H, dtype=torch.float32, device=q.device)
+    ws = _workspace(L.query("dsalt_train_attention_fwd_workspace_bytes", T, H, S, kl), q.device)
     L.call("dsalt_train_attention_fwd", _ptr(qc), _ptr(kc), _ptr(vc), _dt(qc), T, H, n_kv, D, qc.stride(0),
            kc.stride(0), _ptr(w_cont.float().contiguous()), _ptr(lmk_pos.to(torch.int32).contiguous()),
            _ptr(lmk_logw.float().contiguous()), kl, _ptr(_cu_i32(cu_seqlens)), S, float(tau_win), float(win_edge),
-           _ptr(out), _dt(out), _ptr(lse), _stream())
+           _ptr(out), _dt(out), _ptr(lse), _ptr(ws), ws.numel(), _stream())
     return out, lse
 
 

@@ -160,22 +160,27 @@ int dsalt_attention_bwd(const void* q, const void* k, const void* v, int dtype, 
  *   _train_bwd_preprocess, _train_bwd_kernel and _train_bwd_dkdv_kernel (:220-490).
  *
  * q [T, n_heads, head_dim], k/v [T, n_kv, head_dim] as for the forward above (any of bf16,
- *   fp16, fp32; CUDA cores, fp32 arithmetic; head_dim 64 or 128). w_cont [T] fp32: the
+ *   fp16, fp32; head_dim 64 or 128). The forward runs bf16 / fp16 inputs with
+ *   0 <= win_edge <= 4 on the tensor cores (P rounded to the input dtype for P·V, as the
+ *   reference's tl.dot; 16-byte aligned rows), everything else on CUDA cores in fp32; the
+ *   backward runs on CUDA cores in fp32. w_cont [T] fp32: the
  *   continuous window widths w̃. lmk [n_heads, n_seqs, k_lmk] int32 positions (one set per
  *   sequence, any slot order, -1 = none) and lmk_logw [n_heads, n_seqs, k_lmk] fp32 their
  *   log-weights log σ(s/τ_lmk). Query i attends to the band 0 <= i - j <= w̃(i) with the soft
  *   edge log σ((w̃ - (i - j)) / tau_win) outside the core i - j <= w̃ - win_edge, and to the
  *   landmarks p < i - w̃, p <= i with logit + log-weight. Forward: out [T, n_heads, head_dim]
- *   in out_dtype, lse [T, n_heads] (natural log; nullable). Backward (workspace from
+ *   in out_dtype, lse [T, n_heads] (natural log; nullable); workspace from
+ *   dsalt_train_attention_fwd_workspace_bytes. Backward (workspace from
  *   dsalt_attention_bwd_workspace_bytes): from out, dout and lse, writes dq, dk, dv
  *   (fp32, as dsalt_attention_bwd), d_logw [n_heads, n_seqs, k_lmk] and d_w [T] (the
  *   gradient of w̃, summed over heads); dk, dv, d_logw and d_w accumulate with atomic adds.
  */
+size_t dsalt_train_attention_fwd_workspace_bytes(int64_t T, int n_heads, int n_seqs, int k_lmk);
 int dsalt_train_attention_fwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads,
                               int n_kv, int head_dim, int64_t q_stride, int64_t kv_stride, const float* w_cont,
                               const int32_t* lmk, const float* lmk_logw, int k_lmk, const int32_t* cu_seqlens,
                               int n_seqs, float tau_win, float win_edge, void* out, int out_dtype, float* lse,
-                              void* stream);
+                              void* workspace, size_t workspace_bytes, void* stream);
 int dsalt_train_attention_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
                               int head_dim, int64_t q_stride, int64_t kv_stride, const void* out, int out_dtype,
                               const void* dout, int dout_dtype, const float* lse, const float* w_cont,
