@@ -9,12 +9,14 @@
 // nothing. Grouped kv heads: head h uses kv head h / (H / H_kv) and its kv gradients add into
 // that head.
 //
-// CUDA cores, fp32 throughout. One CTA per (64-query tile, head), 256 threads; the key axis is
+// CUDA cores, fp32 throughout. One CTA per (64-query tile, head), 128 threads; the key axis is
 // walked in 32-key tiles: the window band of the tile, then the landmark slots of its set.
 // Per key tile the Q/dO tile (resident), the K/V tile and the P/dS tile sit in shared memory
-// with padded rows (stride HD + 1 floats: the 32 banks see distinct rows); every thread
-// computes 2 x 4 (P, dS), 2 rows of dQ and 2 keys of dK / dV (register blocking: ~0.7
-// shared-memory operands per FMA instead of ~1.1).
+// with padded rows (stride HD + 1 floats: the 32 banks see distinct rows). The kernel is
+// bound by shared-memory wavefronts (one per 4-byte load instruction; 16-byte loads cost four
+// and gain nothing), so every thread holds a 4 x 4 register block: 4 rows x 4 keys of P / dS,
+// 4 rows x HD/8 dims of dQ, 4 keys x HD/16 dims of dK and dV (0.5 shared-memory operands per
+// FMA; 0.75 with the 2 x 4 blocks of a 256-thread CTA).
 #include "common.cuh"
 
 namespace dsalt {
@@ -25,7 +27,7 @@ namespace bwd {
 
 constexpr int BM = 64;        // queries per CTA
 constexpr int BN = 32;        // keys per tile
-constexpr int THREADS = 256;
+constexpr int THREADS = 128;
 
 template <int HD>
 struct Smem {
@@ -116,17 +118,16 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
     sdo[r * LD + d] = dov;
   }
   {
-    const int r = tid >> 2, part = tid & 3;  // 4 threads per row
+    const int r = tid >> 1, part = tid & 1;  // 2 threads per row
     const int i = m0 + r;
     float acc = 0.f;
     if (i < L) {
       const int64_t t = seq0 + i;
-      for (int d = part; d < HD; d += 4)
+      for (int d = part; d < HD; d += 2)
         acc += load_elem(p.out, (t * p.H + h) * HD + d, p.out_dtype) * load_elem(p.dout, (t * p.H + h) * HD + d,
                                                                                p.dout_dtype);
     }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     if (part == 0) {
       float l = -INFINITY, wc = 0.f;
       int lo = 0x3fffffff;
@@ -158,11 +159,11 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
   const int32_t* P = p.lmk + ((int64_t)h * n_sets + set) * p.k_lmk;
   const float* Bset = p.lmk_bias ? p.lmk_bias + ((int64_t)h * n_sets + set) * p.k_lmk : nullptr;
 
-  // this thread's share of dQ: rows (tid >> 3) + 32 u, dims (tid & 7) + 8 m at dq_acc[u * HD/8 + m]
-  float dq_acc[HD / 4];
-  float dw_acc[2] = {0.f, 0.f};  // training mode: this thread's part of dL/dw̃ of its two rows
+  // this thread's share of dQ: rows (tid >> 3) + 16 u, dims (tid & 7) + 8 m at dq_acc[u * HD/8 + m]
+  float dq_acc[HD / 2];
+  float dw_acc[4] = {0.f, 0.f, 0.f, 0.f};  // training mode: this thread's part of dL/dw̃ of its rows
 #pragma unroll
-  for (int m = 0; m < HD / 4; ++m) dq_acc[m] = 0.f;
+  for (int m = 0; m < HD / 2; ++m) dq_acc[m] = 0.f;
 
   for (int kt = 0; kt < n_wt + n_lt; ++kt) {
     const bool is_w = kt < n_wt;
@@ -195,31 +196,39 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
       sv[c * LD + d] = vv;
     }
     __syncthreads();
-    // P and dS: thread -> rows rA, rA + 32 and keys c0 + 8 j (2 x 4 entries; per head-dim
-    // step 4 + 8 shared-memory operands for 16 FMAs)
+    // P and dS: thread -> rows rA + 16 u and keys c0 + 8 j (4 x 4 entries; per head-dim
+    // step 8 + 8 shared-memory operands for 32 FMAs)
     {
       const int rA = tid >> 3, c0 = tid & 7;
-      float sacc[2][4], dpacc[2][4];
+      float sacc[4][4], dpacc[4][4];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int j = 0; j < 4; ++j) sacc[u][j] = dpacc[u][j] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
       for (int d = 0; d < HD; ++d) {
-        const float a0 = sq[rA * LD + d], a1 = sq[(rA + 32) * LD + d];
-        const float b0 = sdo[rA * LD + d], b1 = sdo[(rA + 32) * LD + d];
+        float a[4], b[4], kv[4], vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          a[u] = sq[(rA + 16 * u) * LD + d];
+          b[u] = sdo[(rA + 16 * u) * LD + d];
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float kv = sk[(c0 + 8 * j) * LD + d], vv = sv[(c0 + 8 * j) * LD + d];
-          sacc[0][j] = fmaf(a0, kv, sacc[0][j]);
-          sacc[1][j] = fmaf(a1, kv, sacc[1][j]);
-          dpacc[0][j] = fmaf(b0, vv, dpacc[0][j]);
-          dpacc[1][j] = fmaf(b1, vv, dpacc[1][j]);
+          kv[j] = sk[(c0 + 8 * j) * LD + d];
+          vv[j] = sv[(c0 + 8 * j) * LD + d];
         }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            sacc[u][j] = fmaf(a[u], kv[j], sacc[u][j]);
+            dpacc[u][j] = fmaf(b[u], vv[j], dpacc[u][j]);
+          }
       }
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int r = rA + 32 * u;
+      for (int u = 0; u < 4; ++u) {
+        const int r = rA + 16 * u;
         const int i = m0 + r;
         const bool ok = row_ok[r];
         const int lo = row_lo[r];
@@ -257,45 +266,52 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
       }
     }
     __syncthreads();
-    // dQ += dS · K (dS = rec · scale): thread -> rows rA, rA + 32 and dims d0 + 8 m
+    // dQ += dS · K (dS = rec · scale): thread -> rows rA + 16 u and dims d0 + 8 m
     {
       const int rA = tid >> 3, d0 = tid & 7;
-#pragma unroll 4
+#pragma unroll 2
       for (int c = 0; c < BN; ++c) {
-        const float ds0 = sds[rA * (BN + 1) + c] * p.scale, ds1 = sds[(rA + 32) * (BN + 1) + c] * p.scale;
+        float ds[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) ds[u] = sds[(rA + 16 * u) * (BN + 1) + c] * p.scale;
 #pragma unroll
         for (int m = 0; m < HD / 8; ++m) {
           const float kv = sk[c * LD + d0 + 8 * m];
-          dq_acc[m] = fmaf(ds0, kv, dq_acc[m]);
-          dq_acc[HD / 8 + m] = fmaf(ds1, kv, dq_acc[HD / 8 + m]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) dq_acc[u * (HD / 8) + m] = fmaf(ds[u], kv, dq_acc[u * (HD / 8) + m]);
         }
       }
     }
-    // dK_tile = dSᵀ · Q, dV_tile = Pᵀ · dO: thread -> keys kA, kA + 16 and dims d0 + 16 m
+    // dK_tile = dSᵀ · Q, dV_tile = Pᵀ · dO: thread -> keys kA + 8 u and dims d0 + 16 m
     {
       const int kA = tid >> 4, d0 = tid & 15;
       constexpr int ND = HD / 16;
-      float dkacc[2][ND], dvacc[2][ND];
+      float dkacc[4][ND], dvacc[4][ND];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int m = 0; m < ND; ++m) dkacc[u][m] = dvacc[u][m] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
       for (int r = 0; r < BM; ++r) {
-        const float ds0 = sds[r * (BN + 1) + kA] * p.scale, ds1 = sds[r * (BN + 1) + kA + 16] * p.scale;
-        const float p0 = sp[r * (BN + 1) + kA], p1 = sp[r * (BN + 1) + kA + 16];
+        float ds[4], pr[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          ds[u] = sds[r * (BN + 1) + kA + 8 * u] * p.scale;
+          pr[u] = sp[r * (BN + 1) + kA + 8 * u];
+        }
 #pragma unroll
         for (int m = 0; m < ND; ++m) {
           const float qv = sq[r * LD + d0 + 16 * m], dov = sdo[r * LD + d0 + 16 * m];
-          dkacc[0][m] = fmaf(ds0, qv, dkacc[0][m]);
-          dkacc[1][m] = fmaf(ds1, qv, dkacc[1][m]);
-          dvacc[0][m] = fmaf(p0, dov, dvacc[0][m]);
-          dvacc[1][m] = fmaf(p1, dov, dvacc[1][m]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            dkacc[u][m] = fmaf(ds[u], qv, dkacc[u][m]);
+            dvacc[u][m] = fmaf(pr[u], dov, dvacc[u][m]);
+          }
         }
       }
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int pos = key_pos[kA + 16 * u];
+      for (int u = 0; u < 4; ++u) {
+        const int pos = key_pos[kA + 8 * u];
         if (pos >= 0) {
           float* gk = p.dk + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
           float* gv = p.dv + ((seq0 + pos) * (int64_t)p.Hkv + hk) * HD;
@@ -317,21 +333,21 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
     __syncthreads();
   }
   if constexpr (TRAIN) {
-    // dL/dw̃ per row: the 8 threads of a row pair hold parts of it (lanes 8k .. 8k+7)
+    // dL/dw̃ per row: the 8 threads of a row group hold parts of it (lanes 8k .. 8k+7)
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < 4; ++u) {
       float v = dw_acc[u];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
       v += __shfl_xor_sync(0xffffffffu, v, 4);
-      const int r = (tid >> 3) + 32 * u;
+      const int r = (tid >> 3) + 16 * u;
       if ((tid & 7) == 0 && m0 + r < L && v != 0.f) atomicAdd(p.d_w + seq0 + m0 + r, v);
     }
   }
   // dQ of this thread's rows and dims
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int r = (tid >> 3) + 32 * u, d0 = tid & 7;
+  for (int u = 0; u < 4; ++u) {
+    const int r = (tid >> 3) + 16 * u, d0 = tid & 7;
     const int i = m0 + r;
     if (i < L) {
       float* g = p.dq + ((seq0 + i) * (int64_t)p.H + h) * HD;
