@@ -44,7 +44,9 @@ const char* dsalt_last_error(void);
 int dsalt_version(void);
 
 /* Reads (and clears, when `clear` != 0) the device status word that kernels set when a
- * bounded wait gives up. Synchronises `stream`. 0 = no error. */
+ * bounded wait gives up. Synchronises `stream`. 0 = no error. The device addresses of this
+ * word and of the no-allocation scratch array are looked up once per device and kept for
+ * the life of the process: do not use the library across a cudaDeviceReset. */
 int dsalt_device_status(int* status_out, int clear, void* stream);
 /* Queues a copy of the device status word into host memory `status_host` (page-locked, so
  * that the copy is asynchronous) on `stream` and returns without synchronising; the value
