@@ -9,14 +9,15 @@
 // nothing. Grouped kv heads: head h uses kv head h / (H / H_kv) and its kv gradients add into
 // that head.
 //
-// CUDA cores, fp32 throughout. One CTA per (64-query tile, head), 128 threads; the key axis is
-// walked in 32-key tiles: the window band of the tile, then the landmark slots of its set.
-// Per key tile the Q/dO tile (resident), the K/V tile and the P/dS tile sit in shared memory
-// with padded rows (stride HD + 1 floats: the 32 banks see distinct rows). The kernel is
-// bound by shared-memory wavefronts (one per 4-byte load instruction; 16-byte loads cost four
-// and gain nothing), so every thread holds a 4 x 4 register block: 4 rows x 4 keys of P / dS,
-// 4 rows x HD/8 dims of dQ, 4 keys x HD/16 dims of dK and dV (0.5 shared-memory operands per
-// FMA; 0.75 with the 2 x 4 blocks of a 256-thread CTA).
+// S = Q·Kᵀ and dP = dO·Vᵀ on the tensor cores (mma.sync, fp32 accumulate) for 16-bit inputs,
+// on CUDA cores otherwise; everything else on CUDA cores in fp32. One CTA per (64-query tile,
+// head), 128 threads; the key axis is walked in 32-key tiles: the window band of the tile,
+// then the landmark slots of its set. Per key tile the Q/dO tile (resident), the K/V tile and
+// the P/dS tile sit in shared memory with padded rows (stride HD + 8 floats, for
+// conflict-free 8-byte fragment loads). The CUDA-core phases are bound by shared-memory
+// wavefronts (one per 4-byte load instruction; 16-byte loads cost four and gain nothing), so
+// every thread holds a 4 x 4 register block: 4 rows x 4 keys of P / dS, 4 rows x HD/8 dims of
+// dQ, 4 keys x HD/16 dims of dK and dV (0.5 shared-memory operands per FMA).
 #include "common.cuh"
 
 namespace dsalt {
@@ -31,7 +32,7 @@ constexpr int THREADS = 128;
 
 template <int HD>
 struct Smem {
-  static constexpr int LD = HD + 1;  // padded row stride (floats)
+  static constexpr int LD = HD + 8;  // padded row stride (floats): ≡ 8 mod 32
   static constexpr int Q_OFF = 0, DO_OFF = BM * LD, K_OFF = 2 * BM * LD, V_OFF = K_OFF + BN * LD;
   static constexpr int P_OFF = V_OFF + BN * LD, DS_OFF = P_OFF + BM * (BN + 1);
   static constexpr int FLOATS = DS_OFF + BM * (BN + 1);
@@ -70,7 +71,37 @@ struct Params {
   float* d_w;
 };
 
-template <int HD, bool TRAIN>
+// two consecutive fp32 tile values (16-bit input values, so exact) packed as a 16-bit pair
+template <int MT>
+__device__ __forceinline__ uint32_t pack2(const float* a) {
+  const float2 v = *reinterpret_cast<const float2*>(a);
+  uint32_t r;
+  if constexpr (MT == DSALT_BF16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+    memcpy(&r, &h, 4);
+  } else {
+    const __half2 h = __floats2half2_rn(v.x, v.y);
+    memcpy(&r, &h, 4);
+  }
+  return r;
+}
+// d += a · b, one m16n8k16 tile, fp32 accumulate (PTX ISA fragment layouts)
+template <int MT>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  if constexpr (MT == DSALT_BF16) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+  } else {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+  }
+}
+
+template <int HD, bool TRAIN, int MT>  // MT: 0 CUDA cores, DSALT_BF16 / DSALT_F16 tensor-core S and dP
 __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
   using SM = Smem<HD>;
   constexpr int LD = SM::LD;
@@ -196,9 +227,80 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
       sv[c * LD + d] = vv;
     }
     __syncthreads();
-    // P and dS: thread -> rows rA + 16 u and keys c0 + 8 j (4 x 4 entries; per head-dim
-    // step 8 + 8 shared-memory operands for 32 FMAs)
-    {
+    // P and dS of one (row, key) from its logit s = q·k and dp = dO·v; returns rec · d(edge
+    // bias)/dw̃ for the width gradient (training mode)
+    auto emit = [&](int r, int c, float sv_, float dpv) -> float {
+      const int i = m0 + r;
+      const int pos = key_pos[c];
+      const float wc = row_wc[r];
+      bool valid = row_ok[r] && pos >= 0;
+      float logit = sv_ * p.scale;
+      float dbdw = 0.f;  // training mode: d(edge bias)/dw̃ of this window key
+      if (is_w) {
+        if constexpr (TRAIN) {
+          const float d = (float)(i - pos);
+          valid = valid && pos <= i && d <= wc;
+          if (valid && !(d <= wc - p.win_edge)) {
+            const float z = (wc - d) / p.tau;
+            logit += -logf(1.0f + expf(-z));  // log σ(z)
+            dbdw = (1.0f - 1.0f / (1.0f + expf(-z))) / p.tau;
+          }
+        } else {
+          valid = valid && pos >= row_lo[r] && pos <= i;
+        }
+      } else {
+        if constexpr (TRAIN) valid = valid && pos <= i && (float)pos < (float)i - wc;
+        else valid = valid && pos <= i && pos < row_lo[r];
+        if (valid && Bset) logit += Bset[key_slot[c]];
+      }
+      const float pr = valid ? expf(logit - row_lse[r]) : 0.f;
+      const float rec = pr * (dpv - row_delta[r]);
+      sp[r * (BN + 1) + c] = pr;
+      sds[r * (BN + 1) + c] = rec;  // scaled below where dS is used
+      return rec * dbdw;
+    };
+    if constexpr (MT != 0) {
+      // S = Q·Kᵀ and dP = dO·Vᵀ on the tensor cores (mma.sync m16n8k16, fp32 accumulate):
+      // warp w -> rows 16 w .. 16 w + 15, all 32 keys (four n8 tiles). Operands are the
+      // 16-bit input values, exact in the fp32 tiles; fragments by 8-byte loads (row stride
+      // HD + 8: a half warp's 16 loads hit distinct bank pairs).
+      const int w = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3, rw = 16 * w;
+      float sacc[4][4], dpacc[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sacc[j][e] = dpacc[j][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < HD; kk += 16) {
+        uint32_t qa[4], da[4];
+        qa[0] = pack2<MT>(sq + (rw + g) * LD + kk + 2 * t4);
+        qa[1] = pack2<MT>(sq + (rw + g + 8) * LD + kk + 2 * t4);
+        qa[2] = pack2<MT>(sq + (rw + g) * LD + kk + 2 * t4 + 8);
+        qa[3] = pack2<MT>(sq + (rw + g + 8) * LD + kk + 2 * t4 + 8);
+        da[0] = pack2<MT>(sdo + (rw + g) * LD + kk + 2 * t4);
+        da[1] = pack2<MT>(sdo + (rw + g + 8) * LD + kk + 2 * t4);
+        da[2] = pack2<MT>(sdo + (rw + g) * LD + kk + 2 * t4 + 8);
+        da[3] = pack2<MT>(sdo + (rw + g + 8) * LD + kk + 2 * t4 + 8);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t kb[2] = {pack2<MT>(sk + (8 * j + g) * LD + kk + 2 * t4),
+                                  pack2<MT>(sk + (8 * j + g) * LD + kk + 2 * t4 + 8)};
+          const uint32_t vb[2] = {pack2<MT>(sv + (8 * j + g) * LD + kk + 2 * t4),
+                                  pack2<MT>(sv + (8 * j + g) * LD + kk + 2 * t4 + 8)};
+          mma16816<MT>(sacc[j], qa, kb);
+          mma16816<MT>(dpacc[j], da, vb);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x = emit(rw + g + 8 * (e >> 1), 8 * j + 2 * t4 + (e & 1), sacc[j][e], dpacc[j][e]);
+          if constexpr (TRAIN) dw_acc[e >> 1] += x;
+        }
+    } else {
+      // CUDA cores: thread -> rows rA + 16 u and keys c0 + 8 j (4 x 4 entries; per head-dim
+      // step 8 + 8 shared-memory operands for 32 FMAs)
       const int rA = tid >> 3, c0 = tid & 7;
       float sacc[4][4], dpacc[4][4];
 #pragma unroll
@@ -227,43 +329,12 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
           }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int r = rA + 16 * u;
-        const int i = m0 + r;
-        const bool ok = row_ok[r];
-        const int lo = row_lo[r];
-        const float l = row_lse[r], dl = row_delta[r], wc = row_wc[r];
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int c = c0 + 8 * j;
-          const int pos = key_pos[c];
-          bool valid = ok && pos >= 0;
-          float logit = sacc[u][j] * p.scale;
-          float dbdw = 0.f;  // training mode: d(edge bias)/dw̃ of this window key
-          if (is_w) {
-            if constexpr (TRAIN) {
-              const float d = (float)(i - pos);
-              valid = valid && pos <= i && d <= wc;
-              if (valid && !(d <= wc - p.win_edge)) {
-                const float z = (wc - d) / p.tau;
-                logit += -logf(1.0f + expf(-z));          // log σ(z)
-                dbdw = (1.0f - 1.0f / (1.0f + expf(-z))) / p.tau;
-              }
-            } else {
-              valid = valid && pos >= lo && pos <= i;
-            }
-          } else {
-            if constexpr (TRAIN) valid = valid && pos <= i && (float)pos < (float)i - wc;
-            else valid = valid && pos <= i && pos < lo;
-            if (valid && Bset) logit += Bset[key_slot[c]];
-          }
-          const float pr = valid ? expf(logit - l) : 0.f;
-          const float rec = pr * (dpacc[u][j] - dl);
-          sp[r * (BN + 1) + c] = pr;
-          sds[r * (BN + 1) + c] = rec;  // scaled below where dS is used
-          if constexpr (TRAIN) dw_acc[u] = fmaf(rec, dbdw, dw_acc[u]);
+          const float x = emit(rA + 16 * u, c0 + 8 * j, sacc[u][j], dpacc[u][j]);
+          if constexpr (TRAIN) dw_acc[u] += x;
         }
-      }
     }
     __syncthreads();
     // dQ += dS · K (dS = rec · scale): thread -> rows rA + 16 u and dims d0 + 8 m
@@ -333,15 +404,18 @@ __global__ void __launch_bounds__(THREADS) attn_bwd_kernel(const Params p) {
     __syncthreads();
   }
   if constexpr (TRAIN) {
-    // dL/dw̃ per row: the 8 threads of a row group hold parts of it (lanes 8k .. 8k+7)
+    // dL/dw̃ per row: the threads sharing a row hold parts of it (tensor-core path: rows
+    // 16 w + (lane >> 2) + 8 u over lanes 4k .. 4k+3; CUDA cores: rows (tid >> 3) + 16 u over
+    // lanes 8k .. 8k+7)
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < (MT != 0 ? 2 : 4); ++u) {
       float v = dw_acc[u];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      const int r = (tid >> 3) + 16 * u;
-      if ((tid & 7) == 0 && m0 + r < L && v != 0.f) atomicAdd(p.d_w + seq0 + m0 + r, v);
+      if constexpr (MT == 0) v += __shfl_xor_sync(0xffffffffu, v, 4);
+      const int r = MT != 0 ? 16 * (tid >> 5) + ((tid & 31) >> 2) + 8 * u : (tid >> 3) + 16 * u;
+      if (MT != 0 && (tid & 3) != 0) continue;
+      if ((MT != 0 || (tid & 7) == 0) && m0 + r < L && v != 0.f) atomicAdd(p.d_w + seq0 + m0 + r, v);
     }
   }
   // dQ of this thread's rows and dims
@@ -418,8 +492,22 @@ int launch_attn_bwd(const void* q, const void* k, const void* v, int dtype, int6
   p.win_edge = win_edge;
   p.d_w = d_w;
   const int64_t max_tiles = T / BM + n_seqs;
-  auto kern = train ? (HD == 64 ? attn_bwd_kernel<64, true> : attn_bwd_kernel<128, true>)
-                    : (HD == 64 ? attn_bwd_kernel<64, false> : attn_bwd_kernel<128, false>);
+  // tensor-core S and dP when q/k/v and dO are the same 16-bit type (their values are exact
+  // as MMA operands); otherwise CUDA cores
+  const int mt = (dtype == DSALT_BF16 || dtype == DSALT_F16) && dout_dtype == dtype ? dtype : 0;
+  void (*kern)(const Params);
+#define DSALT_BWD_PICK(HD_, TR_)                                                        \
+  kern = mt == DSALT_BF16 ? attn_bwd_kernel<HD_, TR_, DSALT_BF16>                      \
+                          : (mt == DSALT_F16 ? attn_bwd_kernel<HD_, TR_, DSALT_F16>    \
+                                             : attn_bwd_kernel<HD_, TR_, 0>)
+  if (HD == 64) {
+    if (train) DSALT_BWD_PICK(64, true);
+    else DSALT_BWD_PICK(64, false);
+  } else {
+    if (train) DSALT_BWD_PICK(128, true);
+    else DSALT_BWD_PICK(128, false);
+  }
+#undef DSALT_BWD_PICK
   const size_t smem = HD == 64 ? Smem<64>::BYTES : Smem<128>::BYTES;
   if ((rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                        "attention backward smem attr")))
