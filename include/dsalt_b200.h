@@ -144,8 +144,10 @@ int dsalt_attention_fwd(const void* q, const void* k, const void* v, int dtype, 
  *   log, -inf for rows with no key). Outputs (fp32, overwritten): dq [T, n_heads, head_dim],
  *   dk / dv [T, n_kv, head_dim] (summed over the heads of each kv group), d_bias
  *   [n_heads, n_sets, k_lmk] (nullable). head_dim 64 or 128; lmk_block a multiple of 64.
- *   CUDA cores in fp32; dk, dv and d_bias accumulate with atomic adds, so their last bits
- *   vary from run to run.
+ *   S = q·kᵀ and dO·vᵀ on the tensor cores (mma.sync, fp32 accumulate) when q/k/v and dout
+ *   share a 16-bit dtype, on CUDA cores otherwise; the gradient products on CUDA cores in
+ *   fp32; dk, dv and d_bias accumulate with atomic adds, so their last bits vary from run to
+ *   run.
  */
 size_t dsalt_attention_bwd_workspace_bytes(int64_t T, int n_seqs);
 int dsalt_attention_bwd(const void* q, const void* k, const void* v, int dtype, int64_t T, int n_heads, int n_kv,
@@ -165,7 +167,7 @@ int dsalt_attention_bwd(const void* q, const void* k, const void* v, int dtype, 
  *   fp16, fp32; head_dim 64 or 128). The forward runs bf16 / fp16 inputs with
  *   0 <= win_edge <= 4 on the tensor cores (P rounded to the input dtype for P·V, as the
  *   reference's tl.dot; 16-byte aligned rows), everything else on CUDA cores in fp32; the
- *   backward runs on CUDA cores in fp32. w_cont [T] fp32: the
+ *   backward as dsalt_attention_bwd. w_cont [T] fp32: the
  *   continuous window widths w̃. lmk [n_heads, n_seqs, k_lmk] int32 positions (one set per
  *   sequence, any slot order, -1 = none) and lmk_logw [n_heads, n_seqs, k_lmk] fp32 their
  *   log-weights log σ(s/τ_lmk). Query i attends to the band 0 <= i - j <= w̃(i) with the soft
