@@ -172,12 +172,18 @@ class DSALTAttention(nn.Module):
                                                          alpha.detach().float(), w_disc, cu_seqlens, self.k_lmk,
                                                          self.n_min, total_len, cu_h, head_dim=D)
         scores = hybrid_scores_per_head(x, self.v_proj.weight, alpha, H, D)              # [T, H]
-        starts = torch.tensor(cu_h[:-1], dtype=torch.long, device=x.device)
-        abs_pos = starts[None, :, None] + lmk_pos.clamp(min=0)                           # [H, S, k]
-        s_sel = scores[abs_pos, torch.arange(H, device=x.device)[:, None, None]]
+        return w_cont, lmk_pos, self._landmark_logw(scores, lmk_pos, cu_h)
+
+    def _landmark_logw(self, scores, lmk_pos, cu_h):
+        """``log σ(s/τ_lmk)`` of each selected landmark's hybrid score, ``-inf`` in empty slots
+        (``_train_selectors`` ``:481-486``): ``scores [T, H]``, ``lmk_pos [H, S, k]`` positions
+        within each sequence, ``cu_h`` the host list of ``cu_seqlens``."""
+        H = self.n_heads
+        starts = torch.tensor(cu_h[:-1], dtype=torch.long, device=scores.device)
+        abs_pos = starts[None, :, None] + lmk_pos.long().clamp(min=0)                    # [H, S, k]
+        s_sel = scores[abs_pos, torch.arange(H, device=scores.device)[:, None, None]]
         lmk_logw = torch.log(torch.sigmoid(s_sel / self.tau_lmk).clamp(min=1e-20))
-        lmk_logw = torch.where(lmk_pos >= 0, lmk_logw, torch.full_like(lmk_logw, float("-inf")))
-        return w_cont, lmk_pos, lmk_logw
+        return torch.where(lmk_pos >= 0, lmk_logw, torch.full_like(lmk_logw, float("-inf")))
 
     @torch.no_grad()
     def _packed(self, x, cu_seqlens, total_len, device, rope_cs=None, cu_list=None):

@@ -66,3 +66,47 @@ def test_oracle_train_backward_matches_autograd(H, Hkv):
     (o * torch.tensor(dout)).sum().backward()
     for got, ref in ((dq, tq.grad), (dk, tk.grad), (dv, tv.grad), (dlw, tl.grad), (dw, tw.grad)):
         np.testing.assert_allclose(got, ref.numpy(), atol=1e-10)
+
+
+_GOLDEN = __import__("pathlib").Path(__file__).parent / "golden" / "train_ref.npz"
+
+
+@pytest.mark.parametrize("case", ["mha", "gqa"])
+def test_oracle_train_matches_reference_fixture(case):
+    """The oracle against the reference's own dense training attention
+    (``_dense_logbias_from_kernel`` + SDPA, as ``_packed_train`` runs it) on the reference's
+    own selectors (``_train_selectors``): output, and the gradients of q, k, v (per kv
+    head), the continuous widths and the landmark log-weights (fixture from
+    ``tests/golden/make_golden_train.py``, fp32 on CPU; the oracle is float64)."""
+    z = np.load(_GOLDEN)
+    f = lambda n: z[f"{case}/{n}"]  # noqa: E731
+    cu = f("cu").tolist()
+    tau, edge = float(f("tau")), float(f("edge"))
+    q, k, v = (f(n).astype(np.float64) for n in ("q", "k", "v"))
+    lmk, logw, w = f("lmk_pos"), f("lmk_logw").astype(np.float64), f("w_cont")
+    out, lse = O.train_attention_forward(q, k, v, lmk, logw, w, cu, tau, edge)
+    ref = f("out")
+    assert np.abs(out - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max())
+    got = O.train_attention_backward(q, k, v, out, f("dout").astype(np.float64), lse, lmk, logw, w, cu, tau, edge)
+    for name, g in zip(("dq", "dk", "dv", "d_logw", "d_w"), got):
+        r = f(name)
+        err = float(np.abs(g - r).max())
+        assert err <= 1e-4 * max(1.0, float(np.abs(r).max())), f"{case} {name}: {err:.3e}"
+
+
+@pytest.mark.parametrize("case", ["mha", "gqa"])
+def test_module_landmark_logw_matches_reference_fixture(case):
+    """The training module's hybrid scores and landmark log-weights (the torch half of
+    ``DSALTAttention._train_selectors``; the positions come from the CUDA selection) equal
+    the reference's on its own inputs and positions, bit for bit."""
+    from dsalt_b200.module import DSALTAttention, hybrid_scores_per_head
+    z = np.load(_GOLDEN)
+    f = lambda n: torch.from_numpy(z[f"{case}/{n}"])  # noqa: E731
+    scores_ref, lmk = f("scores"), f("lmk_pos")
+    H = scores_ref.shape[1]
+    dm = f("x").shape[1]
+    sc = hybrid_scores_per_head(f("x"), f("v_proj_weight"), f("alpha"), H, dm // H)
+    assert torch.equal(sc, scores_ref)
+    m = DSALTAttention(dm, H, 1, 2, lmk.shape[-1], 8, n_kv_heads=f("v").shape[1])
+    assert m.tau_lmk == float(f("tau_lmk"))
+    assert torch.equal(m._landmark_logw(scores_ref, lmk, f("cu").tolist()), f("lmk_logw"))
