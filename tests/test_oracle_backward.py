@@ -71,3 +71,23 @@ def test_oracle_backward_matches_autograd(H, Hkv, lmk_block, with_bias):
     np.testing.assert_allclose(dk, tk.grad.numpy(), atol=1e-10)
     np.testing.assert_allclose(dv, tv.grad.numpy(), atol=1e-10)
     np.testing.assert_allclose(db, tb.grad.numpy(), atol=1e-10)
+
+
+def test_oracle_backward_matches_reference_fixture():
+    """The oracle's backward against autograd through the reference's PyTorch restatement
+    of its kernel (``_block_attention``, one landmark set per query block; fixture from
+    ``tests/golden/make_golden_backward.py``, fp32 on CPU; the oracle is float64)."""
+    import pathlib
+    z = np.load(pathlib.Path(__file__).parent / "golden" / "bwd_ref.npz")
+    q, k, v = (z[n].astype(np.float64) for n in ("q", "k", "v"))
+    L = q.shape[0]
+    block = int(z["block"])
+    out, lse = O.attention_forward(q, k, v, z["w"], z["lmk"], [0, L], lmk_block=block)
+    ref = z["out"]
+    assert np.abs(out - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max())
+    dq, dk, dv, _ = O.attention_backward(q, k, v, out, z["dout"].astype(np.float64), lse, z["w"], z["lmk"], [0, L],
+                                         lmk_block=block)
+    for name, g in (("dq", dq), ("dk", dk), ("dv", dv)):
+        r = z[name]
+        err = float(np.abs(g - r).max())
+        assert err <= 1e-4 * max(1.0, float(np.abs(r).max())), f"{name}: {err:.3e}"
