@@ -63,3 +63,36 @@ def test_invalid_arguments_are_rejected(lib):
     assert rc == L.ERR_UNSUPPORTED
     st = ctypes.c_int(0)
     assert lib.dsalt_device_status(None, 0, None) == L.ERR_INVALID
+
+
+def test_training_and_backward_arguments_are_rejected(lib):
+    """The training forward / backward and the inference backward validate sizes, dtypes,
+    pointers and (training forward) the workspace before queuing any device work."""
+    fake = ctypes.c_void_p(4096)  # never dereferenced: every call below fails before device work
+    ws_need = lib.dsalt_train_attention_fwd_workspace_bytes(1024, 4, 2, 16)
+    assert ws_need > lib.dsalt_attention_workspace_bytes(1024, 2, 4, 16, 0) and ws_need % 256 == 0
+    assert lib.dsalt_train_attention_fwd_workspace_bytes(1024, 4, 0, 16) == 0
+
+    def train_fwd(T=1024, H=4, Hkv=2, tau=1.0, ptr=fake, ws=fake, ws_bytes=ws_need, dtype=L.BF16):
+        return lib.dsalt_train_attention_fwd(ptr, ptr, ptr, dtype, T, H, Hkv, 64, H * 64, Hkv * 64, ptr, ptr, ptr, 16,
+                                             ptr, 2, tau, 4.0, ptr, L.F32, None, ws, ws_bytes, None)
+
+    assert train_fwd(tau=0.0) == L.ERR_INVALID and b"bad sizes" in lib.dsalt_last_error()
+    assert train_fwd(H=3) == L.ERR_INVALID  # heads not a multiple of the kv heads
+    assert train_fwd(dtype=9) == L.ERR_INVALID
+    assert train_fwd(ptr=None) == L.ERR_INVALID and b"null pointer" in lib.dsalt_last_error()
+    assert train_fwd(ws=None) == L.ERR_INVALID
+    assert train_fwd(ws_bytes=ws_need - 256) == L.ERR_WORKSPACE
+    assert train_fwd(T=0, ptr=None, ws=None) == L.OK  # nothing to do
+
+    rc = lib.dsalt_train_attention_bwd(fake, fake, fake, L.BF16, 1024, 4, 2, 64, 256, 128, fake, L.F32, fake, L.F32,
+                                       fake, fake, fake, fake, 16, fake, 2, -1.0, 4.0, fake, fake, fake, fake, fake,
+                                       fake, 4096, None)
+    assert rc == L.ERR_INVALID and b"bad sizes" in lib.dsalt_last_error()
+    rc = lib.dsalt_train_attention_bwd(fake, fake, fake, L.BF16, 1024, 4, 2, 64, 256, 128, fake, L.F32, fake, L.F32,
+                                       fake, None, fake, fake, 16, fake, 2, 1.0, 4.0, fake, fake, fake, fake, fake,
+                                       fake, 4096, None)
+    assert rc == L.ERR_INVALID and b"null pointer" in lib.dsalt_last_error()
+    rc = lib.dsalt_attention_bwd(fake, fake, fake, L.BF16, 1024, 4, 2, 64, 128, 128, fake, L.F32, fake, L.F32, fake,
+                                 fake, fake, None, 16, 0, 2, fake, 2, fake, fake, fake, None, fake, 4096, None)
+    assert rc == L.ERR_INVALID and b"token stride" in lib.dsalt_last_error()
