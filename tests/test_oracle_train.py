@@ -110,3 +110,22 @@ def test_module_landmark_logw_matches_reference_fixture(case):
     m = DSALTAttention(dm, H, 1, 2, lmk.shape[-1], 8, n_kv_heads=f("v").shape[1])
     assert m.tau_lmk == float(f("tau_lmk"))
     assert torch.equal(m._landmark_logw(scores_ref, lmk, f("cu").tolist()), f("lmk_logw"))
+
+
+def test_module_landmark_logw_empty_slots():
+    """Empty slots (-1) get log-weight -inf; positions index their own sequence's rows."""
+    from dsalt_b200.module import DSALTAttention
+    m = DSALTAttention(16, 2, 1, 8, 3, 8)
+    scores = torch.arange(20, dtype=torch.float32).view(10, 2) / 10  # [T, H], T = 4 + 6
+    lmk = torch.tensor([[[0, 3, -1], [1, -1, -1]], [[2, 2, 0], [5, 0, -1]]])  # [H, S, k]
+    got = m._landmark_logw(scores, lmk, [0, 4, 10])
+    starts = [0, 4]
+    for h in range(2):
+        for s in range(2):
+            for c in range(3):
+                p = int(lmk[h, s, c])
+                if p < 0:
+                    assert got[h, s, c] == float("-inf")
+                else:
+                    ref = math.log(1.0 / (1.0 + math.exp(-float(scores[starts[s] + p, h]) / m.tau_lmk)))
+                    assert abs(float(got[h, s, c]) - ref) < 1e-6
