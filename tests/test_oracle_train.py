@@ -129,3 +129,30 @@ def test_module_landmark_logw_empty_slots():
                 else:
                     ref = math.log(1.0 / (1.0 + math.exp(-float(scores[starts[s] + p, h]) / m.tau_lmk)))
                     assert abs(float(got[h, s, c]) - ref) < 1e-6
+
+
+def test_oracle_train_small_widths_match_autograd():
+    """Widths below the edge width (the whole band is soft edge, w̃ < 1 keeps only the
+    diagonal), landmarks out of range and empty slots: backward against float64 autograd."""
+    rng = np.random.default_rng(5)
+    cu = [0, 40, 70]
+    T, H, D, k_lmk, tau, edge = cu[-1], 2, 8, 6, 0.7, 4
+    q, k, v = (rng.standard_normal((T, H, D)) for _ in range(3))
+    wc = rng.uniform(0.2, 6.0, T).astype(np.float32)
+    lmk = np.full((H, 2, k_lmk), -1, dtype=np.int32)
+    for h in range(H):
+        for s in range(2):
+            lmk[h, s, :4] = rng.choice(30, size=4, replace=False)
+    lmk[0, 1, 4] = 45  # beyond the second sequence's length: never a key
+    logw = rng.standard_normal(lmk.shape) * 0.5
+    out, lse = O.train_attention_forward(q, k, v, lmk, logw, wc, cu, tau, edge)
+    dout = rng.standard_normal(out.shape)
+    got = O.train_attention_backward(q, k, v, out, dout, lse, lmk, logw, wc, cu, tau, edge)
+    tq, tk, tv = (torch.tensor(a, requires_grad=True) for a in (q, k, v))
+    tl = torch.tensor(logw, requires_grad=True)
+    tw = torch.tensor(wc.astype(np.float64), requires_grad=True)
+    o = _dense_train_forward(tq, tk, tv, tl, tw, lmk, cu, tau, edge)
+    np.testing.assert_allclose(o.detach().numpy(), out, atol=1e-12)
+    (o * torch.tensor(dout)).sum().backward()
+    for g, r in zip(got, (tq.grad, tk.grad, tv.grad, tl.grad, tw.grad)):
+        np.testing.assert_allclose(g, r.numpy(), atol=1e-10)
